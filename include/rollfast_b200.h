@@ -1,0 +1,165 @@
+/*
+ * rollfast_b200 -- C ABI of the B200-native Muon update hot path.
+ *
+ * Every entry point is stream-ordered and asynchronous, takes plain device
+ * pointers and sizes, never allocates device memory and never aborts: it
+ * returns an rf_status and keeps a thread-local message for rf_last_error().
+ * The caller owns every buffer (inputs, outputs and the workspace sized by
+ * the *_workspace_size queries).
+ *
+ * The entry points replace the per-leaf work of the reference's Optax
+ * transforms (RhizomeResearch/rollfast, paths relative to its root):
+ *   rf_muon_update          <- scale_by_muon.update_fn + scale_by_shape +
+ *                              add_decayed_weights + scale_by_learning_rate
+ *                              for the Muon branch (src/rollfast/optim/muon.py:225-330,
+ *                              130-137, 390-393, 462-467)
+ *   rf_newton_schulz        <- orthogonalize_via_newton_schulz / quintic_newton_schulz,
+ *                              the `orthogonalize_fn` plugin seam
+ *                              (src/rollfast/optim/orthogonalization.py:211-305)
+ *   rf_adamw_update         <- scale_by_adam.update_fn + add_decayed_weights +
+ *                              scale_by_learning_rate (src/rollfast/optim/adam.py:123-233, 380-404)
+ *   rf_muon_tail            <- scale_by_shape + add_decayed_weights + scale_by_learning_rate
+ *                              applied to gathered orthogonalised leaves (muon.py:130-137, 390-393, 466)
+ * A JAX integration registers these as XLA FFI custom calls; a ctypes
+ * binding (rollfast_b200/_lib.py) is the host used in this repository.
+ */
+#ifndef ROLLFAST_B200_H_
+#define ROLLFAST_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum rf_status {
+  RF_OK = 0,
+  RF_EINVAL = 1,    /* bad shape / dtype / null pointer / too-small workspace */
+  RF_ECUDA = 2,     /* CUDA launch or driver error (message in rf_last_error) */
+  RF_ETIMEOUT = 3,  /* a bounded device-side wait gave up; results invalid */
+  RF_ENOTSUP = 4    /* option outside the supported hot path */
+} rf_status;
+
+typedef enum rf_dtype { RF_F32 = 0, RF_BF16 = 1, RF_F16 = 2 } rf_dtype;
+
+typedef enum rf_accumulator { RF_EMA = 0, RF_HEAVY_BALL = 1 } rf_accumulator;
+
+/* Newton-Schulz operand precision: 16-bit tensor-core operands (fp32
+ * accumulate in TMEM) or a float32 path for reference-grade parity. */
+typedef enum rf_ns_precision { RF_NS_F16 = 0, RF_NS_BF16 = 1, RF_NS_F32 = 2 } rf_ns_precision;
+
+/* One Muon leaf, already in the reference's (batch, reduction, output)
+ * layout (dimension_numbers.py:312-359): a contiguous [batch][rows][cols]
+ * array.  Newton-Schulz runs on the rows x cols matrices, transposed when
+ * rows > cols (orthogonalization.py:228-231). */
+typedef struct rf_muon_leaf {
+  const void* grad;   /* [batch][rows][cols], grad_dtype */
+  float* mu;          /* [batch][rows][cols] fp32 momentum, updated in place */
+  const void* param;  /* [batch][rows][cols], param_dtype; may be NULL when decay == 0 */
+  void* out;          /* [batch][rows][cols], out_dtype: the update (or O when the tail is deferred) */
+  int64_t batch, rows, cols;
+  int32_t grad_dtype, param_dtype, out_dtype;
+  float shape_scale;  /* muon.py:79-100 factor for this leaf */
+  float decay;        /* weight decay for this leaf (0 when masked out) */
+  int32_t skip_ns;    /* 1: this rank does not own the leaf (multi-GPU); momentum/NS skipped */
+} rf_muon_leaf;
+
+typedef struct rf_muon_params {
+  float beta;            /* muon.py:402 */
+  float eps;             /* muon.py:403, Frobenius normaliser epsilon */
+  int32_t count;         /* state.count before this step (0-based) */
+  int32_t nesterov;      /* muon.py:408 */
+  int32_t accumulator;   /* rf_accumulator */
+  int32_t ns_steps;
+  int32_t n_coeff_rows;  /* 1 for a (3,) array, else rows of an (n,3) schedule (>= ns_steps) */
+  const float* coeffs;   /* HOST pointer: n_coeff_rows * 3 floats (a,b,c) */
+  int32_t precision;     /* rf_ns_precision */
+  float lr;              /* learning rate at this step (scale_by_learning_rate) */
+  int32_t fuse_tail;     /* 1: out = -lr*(scale*O + decay*p); 0: out = O (leaf layout) */
+} rf_muon_params;
+
+/* Bytes of workspace rf_muon_update needs for these leaves and precision. */
+rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision,
+                                 size_t* bytes);
+
+/* Full Muon-branch step for n_leaves leaves: momentum (EMA / heavy-ball,
+ * Nesterov, bias correction), Frobenius normalisation, quintic Newton-Schulz,
+ * and (fuse_tail) shape scale + decoupled decay + learning-rate scale.
+ * Leaves of equal matrix shape are batched into one grouped launch per GEMM. */
+rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Momentum step alone, for a caller-supplied orthogonalize_fn: updates mu in
+ * place and writes the Nesterov / bias-corrected direction (fp32, leaf
+ * layout) to each leaf's `out` (utils.py:565-645; muon.py:240-256). */
+rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
+                            void* stream);
+
+/* The orthogonalize_fn seam: out = NS(x) over [batch][rows][cols]. */
+rf_status rf_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols,
+                                          int32_t precision, size_t* bytes);
+rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
+                           int64_t batch, int64_t rows, int64_t cols, const float* coeffs,
+                           int32_t n_coeff_rows, int32_t ns_steps, float eps, int32_t precision,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Deferred tail for gathered orthogonalised leaves (multi-GPU path):
+ * out = -lr * (shape_scale * O + decay * p), O read from `o` in leaf layout. */
+typedef struct rf_tail_leaf {
+  const void* o;      /* [n] orthogonalised leaf, o_dtype */
+  const void* param;  /* [n], param_dtype, may be NULL when decay == 0 */
+  void* out;          /* [n], out_dtype */
+  int64_t n;
+  int32_t o_dtype, param_dtype, out_dtype;
+  float shape_scale, decay;
+} rf_tail_leaf;
+rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, void* stream);
+
+/* (N)AdamW fallback leaves (adam.py:123-233 + decay + LR). */
+typedef struct rf_adam_leaf {
+  const void* grad;   /* [n], grad_dtype */
+  float* mu;          /* [n] fp32, in place */
+  float* nu;          /* [n] fp32, in place */
+  const void* param;  /* [n], param_dtype; may be NULL when decay == 0 */
+  void* out;          /* [n], out_dtype */
+  int64_t n;
+  int32_t grad_dtype, param_dtype, out_dtype;
+  float decay;
+  /* dtype the product decay * p is rounded to: the parameter dtype for
+   * optax.add_decayed_weights (weakly typed Python float), RF_F32 for the
+   * in-transform decay of scale_by_adam (utils.py:79-90). */
+  int32_t decay_rounding;
+} rf_adam_leaf;
+typedef struct rf_adam_params {
+  float b1, b2, eps, eps_root;
+  int32_t count;      /* state.count before this step */
+  int32_t nesterov;
+  float lr;
+} rf_adam_params;
+rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
+                          void* stream);
+
+/* Diagnostics. */
+const char* rf_last_error(void);
+rf_status rf_version(int32_t* major, int32_t* minor, int32_t* patch);
+/* Number of kernels this library launched in this process (for bench accounting). */
+int64_t rf_kernel_launch_count(void);
+/* Launch profiling of the Newton-Schulz GEMM kernel: while enabled, every
+ * NS GEMM launch is bracketed by CUDA events on its own stream.
+ * rf_profile_end synchronises those events and returns the summed kernel
+ * time, the launch count, and the dense algorithmic FLOPs (X X^T: 2m^2n,
+ * A A: 2m^3, B X: 2m^2n per matrix) and executed FLOPs (symmetric products
+ * visit only tiles that touch the upper triangle) of those launches. */
+rf_status rf_profile_begin(void);
+rf_status rf_profile_end(double* gemm_ms, int64_t* launches, double* algorithmic_flops,
+                         double* executed_flops);
+/* Synchronises `stream`, then reports any sticky CUDA error or a bounded
+ * device-side wait that gave up (RF_ETIMEOUT) since the last check. */
+rf_status rf_sync_check(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ROLLFAST_B200_H_ */

@@ -1,0 +1,202 @@
+"""ctypes binding of ``librollfast_b200.so`` (the C ABI in ``include/rollfast_b200.h``).
+
+This is the same surface an XLA FFI registration would bind; every call
+checks the returned ``rf_status`` and raises with the library's message.
+There is no fallback: if the shared library is missing, importing the
+compute entry points raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "librollfast_b200.so")
+
+RF_OK, RF_EINVAL, RF_ECUDA, RF_ETIMEOUT, RF_ENOTSUP = 0, 1, 2, 3, 4
+RF_F32, RF_BF16, RF_F16 = 0, 1, 2
+RF_EMA, RF_HEAVY_BALL = 0, 1
+RF_NS_F16, RF_NS_BF16, RF_NS_F32 = 0, 1, 2
+
+PRECISIONS = {"f16": RF_NS_F16, "fp16": RF_NS_F16, "float16": RF_NS_F16,
+              "bf16": RF_NS_BF16, "bfloat16": RF_NS_BF16,
+              "f32": RF_NS_F32, "fp32": RF_NS_F32, "float32": RF_NS_F32}
+
+# Exported symbols of include/rollfast_b200.h (checked by the CPU test-suite).
+EXPORTED = (
+    "rf_muon_workspace_size",
+    "rf_muon_update",
+    "rf_muon_direction",
+    "rf_newton_schulz_workspace_size",
+    "rf_newton_schulz",
+    "rf_muon_tail",
+    "rf_adamw_update",
+    "rf_last_error",
+    "rf_version",
+    "rf_kernel_launch_count",
+    "rf_sync_check",
+    "rf_profile_begin",
+    "rf_profile_end",
+)
+
+
+class RfMuonLeaf(ctypes.Structure):
+    _fields_ = [
+        ("grad", ctypes.c_void_p),
+        ("mu", ctypes.c_void_p),
+        ("param", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("batch", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("grad_dtype", ctypes.c_int32),
+        ("param_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("shape_scale", ctypes.c_float),
+        ("decay", ctypes.c_float),
+        ("skip_ns", ctypes.c_int32),
+    ]
+
+
+class RfMuonParams(ctypes.Structure):
+    _fields_ = [
+        ("beta", ctypes.c_float),
+        ("eps", ctypes.c_float),
+        ("count", ctypes.c_int32),
+        ("nesterov", ctypes.c_int32),
+        ("accumulator", ctypes.c_int32),
+        ("ns_steps", ctypes.c_int32),
+        ("n_coeff_rows", ctypes.c_int32),
+        ("coeffs", ctypes.POINTER(ctypes.c_float)),
+        ("precision", ctypes.c_int32),
+        ("lr", ctypes.c_float),
+        ("fuse_tail", ctypes.c_int32),
+    ]
+
+
+class RfTailLeaf(ctypes.Structure):
+    _fields_ = [
+        ("o", ctypes.c_void_p),
+        ("param", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("n", ctypes.c_int64),
+        ("o_dtype", ctypes.c_int32),
+        ("param_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("shape_scale", ctypes.c_float),
+        ("decay", ctypes.c_float),
+    ]
+
+
+class RfAdamLeaf(ctypes.Structure):
+    _fields_ = [
+        ("grad", ctypes.c_void_p),
+        ("mu", ctypes.c_void_p),
+        ("nu", ctypes.c_void_p),
+        ("param", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("n", ctypes.c_int64),
+        ("grad_dtype", ctypes.c_int32),
+        ("param_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32),
+        ("decay", ctypes.c_float),
+        ("decay_rounding", ctypes.c_int32),
+    ]
+
+
+class RfAdamParams(ctypes.Structure):
+    _fields_ = [
+        ("b1", ctypes.c_float),
+        ("b2", ctypes.c_float),
+        ("eps", ctypes.c_float),
+        ("eps_root", ctypes.c_float),
+        ("count", ctypes.c_int32),
+        ("nesterov", ctypes.c_int32),
+        ("lr", ctypes.c_float),
+    ]
+
+
+class RollfastError(RuntimeError):
+    """A non-OK rf_status from the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"rollfast_b200: status {status}: {message}")
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: str | None = None):
+    """Load (once) and return the native library; raise if it is absent."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise ImportError(
+                f"{p} not found: build it with `python -m rollfast_b200.build` "
+                "(there is no non-CUDA implementation of this path)"
+            )
+        lib = ctypes.CDLL(p)
+        vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+        lib.rf_last_error.restype = ctypes.c_char_p
+        lib.rf_last_error.argtypes = []
+        lib.rf_version.argtypes = [ctypes.POINTER(i32)] * 3
+        lib.rf_kernel_launch_count.restype = i64
+        lib.rf_kernel_launch_count.argtypes = []
+        lib.rf_sync_check.argtypes = [vp]
+        lib.rf_profile_begin.argtypes = []
+        lib.rf_profile_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
+                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+        lib.rf_muon_workspace_size.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, i32, ctypes.POINTER(sz)]
+        lib.rf_muon_update.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, ctypes.POINTER(RfMuonParams), vp, sz, vp]
+        lib.rf_muon_direction.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, ctypes.POINTER(RfMuonParams), vp]
+        lib.rf_newton_schulz_workspace_size.argtypes = [i64, i64, i64, i32, ctypes.POINTER(sz)]
+        lib.rf_newton_schulz.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float), i32,
+                                         i32, ctypes.c_float, i32, vp, sz, vp]
+        lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, vp]
+        lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
+        for name in EXPORTED:
+            f = getattr(lib, name)
+            if name not in ("rf_last_error", "rf_kernel_launch_count"):
+                f.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def check(status: int) -> None:
+    if status != RF_OK:
+        msg = load().rf_last_error().decode("utf-8", "replace")
+        if status == RF_EINVAL:
+            raise ValueError(f"rollfast_b200: {msg}")
+        raise RollfastError(status, msg)
+
+
+def version() -> tuple[int, int, int]:
+    a, b, c = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    check(load().rf_version(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)))
+    return a.value, b.value, c.value
+
+
+def kernel_launch_count() -> int:
+    return int(load().rf_kernel_launch_count())
+
+
+def sync_check(stream_handle: int) -> None:
+    check(load().rf_sync_check(ctypes.c_void_p(stream_handle)))
+
+
+def profile_begin() -> None:
+    check(load().rf_profile_begin())
+
+
+def profile_end() -> dict:
+    ms, n = ctypes.c_double(), ctypes.c_int64()
+    alg, exe = ctypes.c_double(), ctypes.c_double()
+    check(load().rf_profile_end(ctypes.byref(ms), ctypes.byref(n), ctypes.byref(alg), ctypes.byref(exe)))
+    return {"gemm_ms": ms.value, "launches": n.value, "algorithmic_flops": alg.value, "executed_flops": exe.value}

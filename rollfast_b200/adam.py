@@ -1,0 +1,194 @@
+"""(N)AdamW fallback (restates src/rollfast/optim/adam.py) on the
+``rf_adamw_update`` kernel."""
+
+from __future__ import annotations
+
+from typing import Any, NamedTuple
+
+import torch
+
+from . import _lib
+from .base import (
+    AddDecayedWeightsState,
+    GradientTransformation,
+    MaskedState,
+    ScaleByScheduleState,
+    ScaleState,
+    has_nonzero_or_scheduled,
+    host_count,
+    new_count,
+    rf_dtype,
+    require_cuda,
+    resolve_mask,
+    resolve_scalar,
+    round_to_dtype,
+    safe_increment,
+    stream_handle,
+)
+from .tree import MaskedNode, is_aux_leaf, tree_flatten, tree_unflatten
+
+
+class ScaleByAdamState(NamedTuple):
+    """adam.py:28-35."""
+
+    count: torch.Tensor
+    mu: Any
+    nu: Any
+    magma_s: Any
+    key: Any
+
+
+def fresh_key(key=None) -> torch.Tensor:
+    """utils.py:73-76: the reference keeps a PRNG key in the state
+    (PRNGKey(42) = [0, 42] by default); the hot path consumes no randomness."""
+    if key is None:
+        return torch.tensor([0, 42], dtype=torch.int64)
+    return torch.as_tensor(key).clone()
+
+
+def zeros_like_tree(params, dtype=torch.float32):
+    """utils.py:25-43."""
+    leaves, treedef = tree_flatten(params, is_leaf=is_aux_leaf)
+    return tree_unflatten(
+        treedef, [x if is_aux_leaf(x) else torch.zeros(x.shape, dtype=dtype, device=x.device) for x in leaves]
+    )
+
+
+def _check_mu_dtype(mu_dtype) -> None:
+    if mu_dtype is not None and mu_dtype not in (torch.float32, "float32", "f32"):
+        raise NotImplementedError(
+            "mu_dtype other than float32 (stochastically rounded bf16 state) is not on the B200 hot path"
+        )
+
+
+def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float) -> None:
+    """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype)."""
+    if not items:
+        return
+    lib = _lib.load()
+    arr = (_lib.RfAdamLeaf * len(items))()
+    for i, (g, mu, nu, p, out, decay, rdt) in enumerate(items):
+        arr[i].grad = g.data_ptr()
+        arr[i].mu = mu.data_ptr()
+        arr[i].nu = nu.data_ptr()
+        arr[i].param = p.data_ptr() if p is not None else None
+        arr[i].out = out.data_ptr()
+        arr[i].n = g.numel()
+        arr[i].grad_dtype = rf_dtype(g)
+        arr[i].param_dtype = rf_dtype(p) if p is not None else _lib.RF_F32
+        arr[i].out_dtype = rf_dtype(out)
+        arr[i].decay = decay
+        arr[i].decay_rounding = rdt
+    prm = _lib.RfAdamParams(float(b1), float(b2), float(eps), float(eps_root), int(count), int(bool(nesterov)),
+                            float(lr))
+    _lib.check(lib.rf_adamw_update(arr, len(items), prm, stream_handle(items[0][0])))
+
+
+def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_rounding_param: bool):
+    """Leaf list for run_adam plus the output tree skeleton."""
+    leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
+    mus = tree_flatten(state.mu, is_leaf=is_aux_leaf)[0]
+    nus = tree_flatten(state.nu, is_leaf=is_aux_leaf)[0]
+    ps = tree_flatten(params, is_leaf=is_aux_leaf)[0] if params is not None else [None] * len(leaves)
+    ms = (tree_flatten(decay_mask, is_leaf=is_aux_leaf)[0] if decay_mask is not None else [True] * len(leaves))
+    items, outs = [], []
+    for g, mu, nu, p, m in zip(leaves, mus, nus, ps, ms):
+        if is_aux_leaf(g):
+            outs.append(g)
+            continue
+        require_cuda(g, "gradient")
+        if g.dtype.is_complex:
+            raise NotImplementedError("complex leaves are not on the B200 hot path")
+        if isinstance(m, torch.Tensor) and m.ndim > 0:
+            raise NotImplementedError("element-wise weight-decay masks are not supported; use per-leaf booleans")
+        use = decay != 0.0 and bool(m) and p is not None and not is_aux_leaf(p)
+        out = torch.empty(g.shape, dtype=torch.float32, device=g.device)
+        if use:
+            rdt = rf_dtype(p) if decay_rounding_param else _lib.RF_F32
+            d = round_to_dtype(decay, p.dtype) if decay_rounding_param else decay
+            items.append((g.contiguous(), mu, nu, p.contiguous(), out, d, rdt))
+        else:
+            items.append((g.contiguous(), mu, nu, None, out, 0.0, _lib.RF_F32))
+        outs.append(out)
+    return items, outs, treedef
+
+
+def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, weight_decay=0.0,
+                  weight_decay_mask=None, nesterov: bool = False, use_magma: bool = False, magma_p: float = 0.5,
+                  magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
+    """adam.py:38-235 (no Magma): returns the Adam direction
+    m_hat / (sqrt(v_hat + eps_root) + eps), plus the in-transform decoupled
+    decay when ``params`` are given (adam.py:185-201)."""
+    if use_magma:
+        raise NotImplementedError("Magma masking is not on the B200 hot path")
+    _check_mu_dtype(mu_dtype)
+    if callable(weight_decay):
+        raise NotImplementedError("scheduled weight_decay is not supported")
+
+    def init_fn(params):
+        return ScaleByAdamState(new_count(0), zeros_like_tree(params), zeros_like_tree(params), (), fresh_key(key))
+
+    def update_fn(updates, state, params=None):
+        if has_nonzero_or_scheduled(weight_decay) and params is None:
+            raise ValueError(
+                "`params` must be provided to `scale_by_adam.update` when "
+                "`weight_decay` is nonzero or scheduled."
+            )
+        count = host_count(state.count)
+        mask = resolve_mask(weight_decay_mask, params) if params is not None else None
+        items, outs, treedef = _adam_items(updates, state, params, decay=float(weight_decay), decay_mask=mask,
+                                           decay_rounding_param=False)
+        run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=count, nesterov=nesterov, lr=-1.0)
+        new_state = ScaleByAdamState(safe_increment(state.count), state.mu, state.nu, state.magma_s, state.key)
+        return tree_unflatten(treedef, outs), new_state
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, weight_decay=1e-4,
+          weight_decay_mask=None, *, nesterov: bool = False, use_magma: bool = False, magma_p: float = 0.5,
+          magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
+    """adam.py:238-404: chain(scale_by_adam, add_decayed_weights, scale_by_learning_rate),
+    executed as one fused kernel per step.  State layout matches the chain:
+    (ScaleByAdamState, [AddDecayedWeightsState], ScaleState | ScaleByScheduleState)."""
+    decay_on = has_nonzero_or_scheduled(weight_decay)
+    if use_magma:
+        raise NotImplementedError("Magma masking is not on the B200 hot path")
+    _check_mu_dtype(mu_dtype)
+    if callable(weight_decay):
+        raise NotImplementedError("scheduled weight_decay is not supported")
+    inner = scale_by_adam(b1, b2, eps, eps_root, mu_dtype, nesterov=nesterov, key=key)
+
+    def init_fn(params):
+        states = [inner.init(params)]
+        if decay_on:
+            wd_state = AddDecayedWeightsState()
+            states.append(MaskedState(wd_state) if weight_decay_mask is not None else wd_state)
+        states.append(ScaleByScheduleState(new_count(0)) if callable(learning_rate) else ScaleState())
+        return tuple(states)
+
+    def update_fn(updates, state, params=None):
+        adam_state = state[0]
+        lr_state = state[-1]
+        if decay_on and params is None:
+            raise ValueError(
+                "You are using a transformation that requires the current value of parameters, "
+                "but you are not passing `params` when calling `update`."
+            )
+        lr = resolve_scalar(learning_rate, host_count(lr_state.count)) if callable(learning_rate) else float(
+            learning_rate)
+        mask = resolve_mask(weight_decay_mask, params) if (decay_on and params is not None) else None
+        items, outs, treedef = _adam_items(updates, adam_state, params,
+                                           decay=float(weight_decay) if decay_on else 0.0, decay_mask=mask,
+                                           decay_rounding_param=True)
+        run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=host_count(adam_state.count),
+                 nesterov=nesterov, lr=lr)
+        new_adam = ScaleByAdamState(safe_increment(adam_state.count), adam_state.mu, adam_state.nu,
+                                    adam_state.magma_s, adam_state.key)
+        new_lr = ScaleByScheduleState(safe_increment(lr_state.count)) if callable(learning_rate) else lr_state
+        return tree_unflatten(treedef, outs), (new_adam, *state[1:-1], new_lr)
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+__all__ = ["ScaleByAdamState", "adamw", "scale_by_adam"]

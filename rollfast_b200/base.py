@@ -1,0 +1,327 @@
+"""Optax-shaped plumbing for the drop-in API.
+
+The reference's transforms are Optax ``GradientTransformation`` objects
+(``init(params) -> state``, ``update(updates, state, params) -> (updates,
+state)``) combined with ``optax.chain`` / ``optax.partition`` and wrapped
+with ``optax.masked`` (muon.py:395, 462-486; adam.py:380-404).  Optax is not
+a dependency here; this module restates the pieces of it the Muon path uses,
+with the same state types, over trees of ``torch.Tensor`` device buffers.
+
+Elementwise transforms (``scale_by_muon_shape``, ``add_decayed_weights``,
+``scale_by_learning_rate``) run through the library's ``rf_muon_tail``
+kernel; nothing on the update path computes with torch ops.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Callable, NamedTuple
+
+import torch
+
+from . import _lib
+from .tree import MaskedNode, is_aux_leaf, tree_flatten, tree_leaves, tree_map, tree_unflatten
+
+Params = Any
+Updates = Any
+ScalarOrSchedule = Any
+
+
+class GradientTransformation(NamedTuple):
+    """optax.GradientTransformation."""
+
+    init: Callable[[Params], Any]
+    update: Callable[..., tuple[Updates, Any]]
+
+
+class EmptyState(NamedTuple):
+    """optax.EmptyState."""
+
+
+class ScaleState(NamedTuple):
+    """State of ``optax.scale`` (constant learning rate)."""
+
+
+class ScaleByScheduleState(NamedTuple):
+    """State of ``optax.scale_by_schedule``: the step count fed to the schedule."""
+
+    count: torch.Tensor
+
+
+class AddDecayedWeightsState(NamedTuple):
+    """State of ``optax.add_decayed_weights``."""
+
+
+class MaskedState(NamedTuple):
+    """State of ``optax.masked``."""
+
+    inner_state: Any
+
+
+class PartitionState(NamedTuple):
+    """State of ``optax.partition``."""
+
+    inner_states: dict
+
+
+NO_PARAMS_MSG = (
+    "You are using a transformation that requires the current value of parameters, "
+    "but you are not passing `params` when calling `update`."
+)
+
+
+def init_empty_state(params: Params) -> EmptyState:
+    del params
+    return EmptyState()
+
+
+def host_count(x) -> int:
+    """Step counters live on the host (int32 CPU tensors) so bias corrections
+    and schedules never synchronise with the device."""
+    return int(x.item()) if isinstance(x, torch.Tensor) else int(x)
+
+
+def new_count(value: int = 0) -> torch.Tensor:
+    return torch.tensor(value, dtype=torch.int32)
+
+
+def safe_increment(count: torch.Tensor) -> torch.Tensor:
+    """optax numerics.safe_increment: saturating int32 increment."""
+    c = host_count(count)
+    return new_count(c + 1 if c < 2**31 - 1 else c)
+
+
+# ---------------------------------------------------------------------------
+# dtype helpers
+# ---------------------------------------------------------------------------
+_RF_DTYPE = {torch.float32: _lib.RF_F32, torch.bfloat16: _lib.RF_BF16, torch.float16: _lib.RF_F16}
+
+
+def rf_dtype(t: torch.Tensor) -> int:
+    try:
+        return _RF_DTYPE[t.dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from exc
+
+
+def round_to_dtype(x: float, dtype: torch.dtype) -> float:
+    """The value of Python float ``x`` once cast to ``dtype`` (JAX weak typing
+    forms ``weight_decay * p`` in the parameter dtype)."""
+    return float(torch.tensor(x, dtype=torch.float32).to(dtype).to(torch.float32))
+
+
+def stream_handle(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA torch.Tensor (the update path runs on the GPU only)")
+
+
+def resolve_scalar(value: ScalarOrSchedule, count: int) -> float:
+    """utils.py:93-102."""
+    return float(value(count)) if callable(value) else float(value)
+
+
+def has_nonzero_or_scheduled(value: ScalarOrSchedule) -> bool:
+    """utils.py:105-111."""
+    if isinstance(value, (int, float)):
+        if value < 0.0:
+            raise ValueError("Scalar optimizer coefficients must be nonnegative.")
+        return value != 0.0
+    return True
+
+
+def validate_positive(name: str, value) -> None:
+    """utils.py:114-120."""
+    if isinstance(value, (int, float)) and value <= 0.0:
+        raise ValueError(f"{name} must be positive, got {value!r}.")
+
+
+def validate_beta(name: str, value) -> None:
+    """utils.py:132-138."""
+    if isinstance(value, (int, float)) and not 0.0 <= value < 1.0:
+        raise ValueError(f"{name} must be in [0, 1), got {value!r}.")
+
+
+def resolve_mask(mask, params) -> Any:
+    """utils.py:155-170."""
+    if mask is None:
+        return None
+    if callable(mask):
+        return mask(params)
+    return mask
+
+
+# ---------------------------------------------------------------------------
+# Combinators (optax._src.combine / wrappers)
+# ---------------------------------------------------------------------------
+
+
+def chain(*transforms: GradientTransformation) -> GradientTransformation:
+    """optax.chain."""
+
+    def init_fn(params):
+        return tuple(t.init(params) for t in transforms)
+
+    def update_fn(updates, state, params=None, **extra):
+        new_state = []
+        for t, s in zip(transforms, state):
+            updates, s = t.update(updates, s, params, **extra)
+            new_state.append(s)
+        return updates, tuple(new_state)
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+def _mask_tree(tree, mask):
+    return tree_map(lambda x, m: x if m else MaskedNode(), tree, mask, is_leaf=is_aux_leaf)
+
+
+def masked(inner: GradientTransformation, mask) -> GradientTransformation:
+    """optax.masked: ``inner`` sees MaskedNode at leaves where mask is False."""
+
+    def init_fn(params):
+        m = mask(params) if callable(mask) else mask
+        return MaskedState(inner.init(_mask_tree(params, m)))
+
+    def update_fn(updates, state, params=None, **extra):
+        m = mask(updates) if callable(mask) else mask
+        mu = _mask_tree(updates, m)
+        mp = None if params is None else _mask_tree(params, m)
+        new_u, new_inner = inner.update(mu, state.inner_state, mp, **extra)
+        merged = tree_map(lambda n, o, k: n if k else o, new_u, updates, m, is_leaf=is_aux_leaf)
+        return merged, MaskedState(new_inner)
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+def partition(transforms: dict, param_labels) -> GradientTransformation:
+    """optax.partition (multi_transform)."""
+
+    def labels_of(tree):
+        return param_labels(tree) if callable(param_labels) else param_labels
+
+    def make_mask(labels, group):
+        return tree_map(lambda lab: lab == group, labels)
+
+    def init_fn(params):
+        labels = labels_of(params)
+        used = set(x for x in tree_leaves(labels) if x is not None)
+        missing = used - set(transforms)
+        if missing:
+            raise ValueError(f"Some parameters have no corresponding transformation: {sorted(missing)}")
+        return PartitionState(
+            {g: masked(t, make_mask(labels, g)).init(params) for g, t in transforms.items()}
+        )
+
+    def update_fn(updates, state, params=None, **extra):
+        labels = labels_of(updates)
+        new_inner = {}
+        for g, t in transforms.items():
+            updates, new_inner[g] = masked(t, make_mask(labels, g)).update(
+                updates, state.inner_states[g], params, **extra
+            )
+        return updates, PartitionState(new_inner)
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+# ---------------------------------------------------------------------------
+# Elementwise transforms on the rf_muon_tail kernel:
+#   out = -lr * (shape_scale * u + decay * p)
+# ---------------------------------------------------------------------------
+
+
+def run_tail(items, lr: float) -> None:
+    """items: list of (u, p_or_None, out, shape_scale, decay)."""
+    if not items:
+        return
+    lib = _lib.load()
+    arr = (_lib.RfTailLeaf * len(items))()
+    for i, (u, p, out, scale, decay) in enumerate(items):
+        arr[i].o = u.data_ptr()
+        arr[i].param = p.data_ptr() if p is not None else None
+        arr[i].out = out.data_ptr()
+        arr[i].n = u.numel()
+        arr[i].o_dtype = rf_dtype(u)
+        arr[i].param_dtype = rf_dtype(p) if p is not None else _lib.RF_F32
+        arr[i].out_dtype = rf_dtype(out)
+        arr[i].shape_scale = scale
+        arr[i].decay = decay
+    _lib.check(lib.rf_muon_tail(arr, len(items), lr, stream_handle(items[0][0])))
+
+
+def _array_leaves(tree):
+    leaves, treedef = tree_flatten(tree, is_leaf=is_aux_leaf)
+    return leaves, treedef
+
+
+def scale_by_learning_rate(learning_rate: ScalarOrSchedule, *, flip_sign: bool = True) -> GradientTransformation:
+    """optax.scale_by_learning_rate: multiplies by -lr (schedule-aware)."""
+    sign = -1.0 if flip_sign else 1.0
+
+    def init_fn(params):
+        return ScaleByScheduleState(new_count(0)) if callable(learning_rate) else ScaleState()
+
+    def update_fn(updates, state, params=None, **extra):
+        if callable(learning_rate):
+            c = host_count(state.count)
+            lr = float(learning_rate(c))
+            new_state = ScaleByScheduleState(safe_increment(state.count))
+        else:
+            lr = float(learning_rate)
+            new_state = state
+        leaves, treedef = _array_leaves(updates)
+        items, outs = [], []
+        for u in leaves:
+            if is_aux_leaf(u):
+                outs.append(u)
+                continue
+            require_cuda(u, "update")
+            o = torch.empty_like(u)
+            items.append((u.contiguous(), None, o, 1.0, 0.0))
+            outs.append(o)
+        run_tail(items, -sign * lr)
+        return tree_unflatten(treedef, outs), new_state
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+def add_decayed_weights(weight_decay: float = 0.0, mask=None) -> GradientTransformation:
+    """optax.add_decayed_weights: ``u + weight_decay * p`` where the product is
+    formed in the parameter dtype (JAX weak typing of the Python float)."""
+    if callable(weight_decay):
+        raise NotImplementedError("scheduled weight_decay in add_decayed_weights is not supported")
+
+    def update_fn(updates, state, params=None, **extra):
+        if params is None:
+            raise ValueError(NO_PARAMS_MSG)
+        leaves, treedef = _array_leaves(updates)
+        pleaves = tree_flatten(params, is_leaf=is_aux_leaf)[0]
+        items, outs = [], []
+        for u, p in zip(leaves, pleaves):
+            if is_aux_leaf(u) or is_aux_leaf(p):
+                outs.append(u)
+                continue
+            require_cuda(u, "update")
+            o = torch.empty(u.shape, dtype=torch.promote_types(u.dtype, p.dtype), device=u.device)
+            items.append((u.contiguous(), p.contiguous(), o, 1.0, round_to_dtype(weight_decay, p.dtype)))
+            outs.append(o)
+        run_tail(items, -1.0)
+        return tree_unflatten(treedef, outs), state
+
+    tx = GradientTransformation(lambda params: AddDecayedWeightsState(), update_fn)
+    if mask is not None:
+        return masked(tx, mask)
+    return tx
+
+
+def apply_updates(params, updates):
+    """optax.apply_updates (outside the timed step; provided for examples)."""
+    return tree_map(
+        lambda p, u: p if is_aux_leaf(u) else (p.float() + u.float()).to(p.dtype),
+        params,
+        updates,
+        is_leaf=is_aux_leaf,
+    )

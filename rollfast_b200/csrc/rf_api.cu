@@ -1,0 +1,582 @@
+// C-ABI entry points of librollfast_b200 (declared in include/rollfast_b200.h).
+//
+// Host orchestration of one Muon-branch step:
+//   1. momentum + direction sum-of-squares (k_momentum_sumsq), per grad dtype,
+//      in launches of <= kMaxLeavesPerLaunch leaves;
+//   2. per-matrix Frobenius scale (k_norm_finalize);
+//   3. leaves grouped by their NS shape (m <= n after the transpose the
+//      reference applies when rows > cols); each group, in sub-batches of at
+//      most kMaxLeavesPerLaunch leaves, gets its padded operand X~0
+//      (k_ns_load) and ns_steps x {X X^T, bA + cA^2, aX + BX} GEMM stages, the
+//      last one writing the update (or O) straight into each leaf.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "rf_kernels.cuh"
+
+namespace rf {
+
+// ---------------------------------------------------------------------------
+// Errors and bookkeeping
+// ---------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+static std::atomic<int64_t> g_launches{0};
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+rf_status fail(rf_status st, const std::string& msg) {
+  set_error(msg);
+  return st;
+}
+rf_status check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return RF_OK;
+}
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+int num_sms() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  cache[dev] = n;
+  return n;
+}
+
+rf_status take_device_error();  // rf_ns_tc.cu
+
+// ---------------------------------------------------------------------------
+// Host-side scalar factors, formed in float32 like the reference.
+// ---------------------------------------------------------------------------
+static float f32_pow(float b, int e) { return float(std::pow(double(b), double(e))); }
+
+static MomentumCoeffs momentum_coeffs(const rf_muon_params& p) {
+  MomentumCoeffs c{};
+  const float beta = p.beta;
+  const int t = p.count + 1;  // utils.py:581
+  c.beta = beta;
+  if (p.accumulator == RF_EMA) {
+    c.s = 1.0f - beta;                                                  // utils.py:333
+    const int k_mu = p.nesterov ? t + 1 : t;                            // utils.py:590-593
+    c.bc_mu = 1.0f - f32_pow(beta, k_mu);                               // utils.py:505
+    c.bc_g = 1.0f - f32_pow(beta, t);
+    c.mode = p.nesterov ? kDirEmaNesterov : kDirEma;
+  } else {
+    c.s = 1.0f;                                                         // utils.py:335
+    c.bc_mu = c.bc_g = 1.0f;                                            // utils.py:503-504
+    c.mode = p.nesterov ? kDirHeavyBallNesterov : kDirHeavyBall;
+  }
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// Plan
+// ---------------------------------------------------------------------------
+struct LeafPlan {
+  int idx;
+  const void* g;
+  float* mu;
+  const void* p;
+  void* out;
+  int64_t batch, rows, cols, m, n;
+  int transposed;
+  int gdt, pdt, odt;
+  float shape_scale, decay;
+  int64_t scale_index;  // first matrix in the scale array
+};
+
+struct GroupPlan {
+  int64_t m, n, mp, np;
+  std::vector<std::vector<int>> subs;  // sub-batches of leaf indices (<= kMaxLeavesPerLaunch)
+};
+
+struct Plan {
+  std::vector<LeafPlan> leaves;
+  std::vector<GroupPlan> groups;
+  int64_t total_mats = 0;
+  int64_t total_chunks = 0;
+  size_t off_partials = 0, off_scale = 0, off_ns = 0, bytes = 0;
+  size_t ns_bytes = 0;  // max over sub-batches
+  int precision = RF_NS_F16;
+};
+
+static size_t ns_elem(int precision) { return precision == RF_NS_F32 ? 4 : 2; }
+
+static int64_t chunks_per_mat(int64_t numel) { return ceil_div(numel, kChunk); }
+
+static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan& P) {
+  if (precision != RF_NS_F16 && precision != RF_NS_BF16 && precision != RF_NS_F32)
+    return fail(RF_EINVAL, "unknown NS precision");
+  P.precision = precision;
+  P.leaves = in;
+  std::map<std::pair<int64_t, int64_t>, int> gindex;
+  std::vector<std::vector<int>> members;
+  for (size_t i = 0; i < P.leaves.size(); ++i) {
+    LeafPlan& L = P.leaves[i];
+    L.scale_index = P.total_mats;
+    P.total_mats += L.batch;
+    P.total_chunks += L.batch * chunks_per_mat(L.rows * L.cols);
+    auto key = std::make_pair(L.m, L.n);
+    auto it = gindex.find(key);
+    if (it == gindex.end()) {
+      gindex[key] = int(members.size());
+      members.emplace_back();
+      GroupPlan gp;
+      gp.m = L.m;
+      gp.n = L.n;
+      gp.mp = round_up(L.m, 256);
+      gp.np = round_up(L.n, 256);
+      P.groups.push_back(gp);
+      members.back().push_back(int(i));
+    } else {
+      members[it->second].push_back(int(i));
+    }
+  }
+  const size_t es = ns_elem(precision);
+  for (size_t gi = 0; gi < P.groups.size(); ++gi) {
+    GroupPlan& gp = P.groups[gi];
+    const auto& mem = members[gi];
+    const int nsub = int(ceil_div(int64_t(mem.size()), kMaxLeavesPerLaunch));
+    const size_t per = (mem.size() + nsub - 1) / nsub;  // even split
+    for (size_t s = 0; s < mem.size(); s += per)
+      gp.subs.emplace_back(mem.begin() + s, mem.begin() + std::min(mem.size(), s + per));
+    for (const auto& sub : gp.subs) {
+      int64_t G = 0;
+      for (int li : sub) G += P.leaves[li].batch;
+      const size_t x = align_up(size_t(G) * gp.mp * gp.np * es, 1024);
+      const size_t a = align_up(size_t(G) * gp.mp * gp.mp * es, 1024);
+      P.ns_bytes = std::max(P.ns_bytes, 2 * x + 2 * a);
+    }
+  }
+  P.off_partials = 0;
+  P.off_scale = align_up(size_t(P.total_chunks) * 4, 1024);
+  P.off_ns = P.off_scale + align_up(size_t(P.total_mats) * 4, 1024);
+  P.bytes = P.off_ns + P.ns_bytes;
+  return RF_OK;
+}
+
+static rf_status validate_leaf(const rf_muon_leaf& l, int i, bool need_out) {
+  const std::string where = "leaf " + std::to_string(i) + ": ";
+  if (l.batch <= 0 || l.rows <= 0 || l.cols <= 0) return fail(RF_EINVAL, where + "batch/rows/cols must be positive");
+  if (!valid_dtype(l.grad_dtype) || !valid_dtype(l.out_dtype)) return fail(RF_EINVAL, where + "bad dtype");
+  if (!l.skip_ns && (!l.grad || !l.mu)) return fail(RF_EINVAL, where + "grad and mu must be non-null");
+  if (need_out && !l.out) return fail(RF_EINVAL, where + "out must be non-null");
+  if (l.decay != 0.f && (!l.param || !valid_dtype(l.param_dtype)))
+    return fail(RF_EINVAL, where + "param (valid dtype) required when decay != 0");
+  return RF_OK;
+}
+
+// Runs steps 1-3 for the leaves of `P` (all have NS work).
+static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
+                              int ns_steps, float eps, int fuse_tail, float lr, void* ws, size_t ws_bytes,
+                              cudaStream_t st) {
+  if (P.leaves.empty()) return RF_OK;
+  if (!ws || ws_bytes < P.bytes)
+    return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
+                               std::to_string(ws_bytes));
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(RF_EINVAL, "workspace must be 256-byte aligned");
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  float* partials = reinterpret_cast<float*>(base + P.off_partials);
+  float* denom = reinterpret_cast<float*>(base + P.off_scale);
+  uint8_t* ns = base + P.off_ns;
+
+  // --- 1+2: momentum / sum of squares, then per-matrix denominators -------
+  // Each launch takes leaves of one grad dtype and its own contiguous range
+  // of partial sums.
+  int64_t chunk_cursor = 0;
+  for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
+    std::vector<int> ids;
+    for (size_t i = 0; i < P.leaves.size(); ++i)
+      if (P.leaves[i].gdt == gdt) ids.push_back(int(i));
+    for (size_t s = 0; s < ids.size(); s += kMaxLeavesPerLaunch) {
+      MomentumLaunch L{};
+      L.c = mc;
+      L.partials = partials + chunk_cursor;
+      int64_t chunks = 0, mats = 0;
+      for (size_t k = s; k < std::min(ids.size(), s + size_t(kMaxLeavesPerLaunch)); ++k) {
+        const LeafPlan& lp = P.leaves[ids[k]];
+        MomentumLeaf& ml = L.leaf[L.n++];
+        ml.g = lp.g;
+        ml.mu = lp.mu;
+        ml.numel = lp.rows * lp.cols;
+        ml.chunk_begin = chunks;
+        ml.mat_begin = mats;
+        ml.scale_index = lp.scale_index;
+        ml.chunks_per_mat = int32_t(chunks_per_mat(ml.numel));
+        const size_t ge = dtype_size(gdt);
+        ml.vec_ok = lp.mu && (ml.numel % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.g) % 16 == 0) &&
+                    (reinterpret_cast<uintptr_t>(lp.mu) % 16 == 0) && ((ml.numel * int64_t(ge)) % 16 == 0);
+        chunks += lp.batch * ml.chunks_per_mat;
+        mats += lp.batch;
+      }
+      L.total_chunks = chunks;
+      L.total_mats = mats;
+      chunk_cursor += chunks;
+      RF_TRY(launch_momentum_sumsq(L, gdt, st));
+      RF_TRY(launch_norm_finalize(L, denom, eps, st));
+    }
+  }
+
+  // --- 3: per shape group, per sub-batch: load + NS iterations -------------
+  const size_t es = ns_elem(P.precision);
+  for (const GroupPlan& gp : P.groups) {
+    const NsScales sc = ns_scales(gp.m, P.precision);
+    for (const auto& sub : gp.subs) {
+      int64_t G = 0;
+      for (int li : sub) G += P.leaves[li].batch;
+      const size_t xbytes = align_up(size_t(G) * gp.mp * gp.np * es, 1024);
+      const size_t abytes = align_up(size_t(G) * gp.mp * gp.mp * es, 1024);
+      uint8_t* X0 = ns;
+      uint8_t* X1 = ns + xbytes;
+      uint8_t* Am = ns + 2 * xbytes;
+      uint8_t* Bm = Am + abytes;
+
+      LoadLaunch ld{};
+      ld.c = mc;
+      ld.mp = gp.mp;
+      ld.np = gp.np;
+      ld.denom = denom;
+      ld.sx = sc.sx;
+      ld.x = X0;
+      ld.group_mats = G;
+      NsGemmArgs ga{};
+      ga.precision = P.precision;
+      ga.G = G;
+      ga.m = gp.m;
+      ga.n = gp.n;
+      ga.mp = gp.mp;
+      ga.np = gp.np;
+      ga.fuse_tail = fuse_tail;
+      ga.neg_lr = -lr;
+      ga.out_scale = 1.0f / sc.sx;
+      int64_t gm = 0;
+      for (int li : sub) {
+        const LeafPlan& lp = P.leaves[li];
+        LoadLeaf& l = ld.leaf[ld.n++];
+        l.g = lp.g;
+        l.mu = lp.mu;
+        l.rows = lp.rows;
+        l.cols = lp.cols;
+        l.group_mat_begin = gm;
+        l.norm_index = lp.scale_index;
+        l.transposed = lp.transposed;
+        l.gdt = lp.gdt;
+        FinalLeaf& f = ga.final_leaf[ga.n_final++];
+        f.out = lp.out;
+        f.p = lp.p;
+        f.group_mat_begin = gm;
+        f.transposed = lp.transposed;
+        f.out_dtype = lp.odt;
+        f.p_dtype = lp.pdt;
+        f.shape_scale = lp.shape_scale;
+        f.decay = lp.decay;
+        gm += lp.batch;
+      }
+      RF_TRY(launch_ns_load(ld, P.precision, st));
+
+      uint8_t* xc = X0;
+      uint8_t* xn = X1;
+      for (int it = 0; it < ns_steps; ++it) {
+        const float* cf = coeffs + 3 * (n_coeff_rows == 1 ? 0 : it);
+        const float ca = cf[0], cb = cf[1], cc = cf[2];
+        // A~ = (sa / sx^2) X~ X~^T
+        ga.stage = kSyrkXXt;
+        ga.a_op = ga.b_op = xc;
+        ga.aux = nullptr;
+        ga.out = Am;
+        ga.alpha = sc.sa / (sc.sx * sc.sx);
+        ga.beta = 0.f;
+        RF_TRY(launch_ns_gemm(ga, st));
+        // B~ = sb (b A + c A A) = (c sb / sa^2) A~ A~ + (b sb / sa) A~
+        ga.stage = kSyrkPoly;
+        ga.a_op = ga.b_op = ga.aux = Am;
+        ga.out = Bm;
+        ga.alpha = cc * sc.sb / (sc.sa * sc.sa);
+        ga.beta = cb * sc.sb / sc.sa;
+        RF_TRY(launch_ns_gemm(ga, st));
+        // X~' = sx (a X + B X) = (1 / sb) B~ X~ + a X~
+        ga.stage = (it == ns_steps - 1) ? kGemmBXFinal : kGemmBX;
+        ga.a_op = Bm;
+        ga.b_op = ga.aux = xc;
+        ga.out = xn;
+        ga.alpha = 1.0f / sc.sb;
+        ga.beta = ca;
+        RF_TRY(launch_ns_gemm(ga, st));
+        std::swap(xc, xn);
+      }
+    }
+  }
+  return RF_OK;
+}
+
+static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vector<LeafPlan>& out,
+                                 bool need_out) {
+  if (n < 0 || (n > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  for (int i = 0; i < n; ++i) {
+    const rf_muon_leaf& l = leaves[i];
+    RF_TRY(validate_leaf(l, i, need_out));
+    if (l.skip_ns) continue;
+    LeafPlan p{};
+    p.idx = i;
+    p.g = l.grad;
+    p.mu = l.mu;
+    p.p = l.param;
+    p.out = l.out;
+    p.batch = l.batch;
+    p.rows = l.rows;
+    p.cols = l.cols;
+    p.transposed = l.rows > l.cols;
+    p.m = std::min(l.rows, l.cols);
+    p.n = std::max(l.rows, l.cols);
+    p.gdt = l.grad_dtype;
+    p.pdt = l.param ? l.param_dtype : RF_F32;
+    p.odt = l.out_dtype;
+    p.shape_scale = l.shape_scale;
+    p.decay = l.decay;
+    out.push_back(p);
+  }
+  return RF_OK;
+}
+
+static rf_status check_coeffs(const float* coeffs, int n_rows, int steps) {
+  if (steps < 1) return fail(RF_EINVAL, "ns_steps must be >= 1");
+  if (!coeffs) return fail(RF_EINVAL, "coeffs must be non-null");
+  if (n_rows < 1) return fail(RF_EINVAL, "n_coeff_rows must be >= 1");
+  if (n_rows > 1 && n_rows < steps) return fail(RF_EINVAL, "Not enough coeffs to perform ns_steps steps");
+  return RF_OK;
+}
+
+}  // namespace rf
+
+using namespace rf;
+
+extern "C" {
+
+const char* rf_last_error(void) { return t_last_error.c_str(); }
+
+rf_status rf_version(int32_t* major, int32_t* minor, int32_t* patch) {
+  if (!major || !minor || !patch) return fail(RF_EINVAL, "null output pointer");
+  *major = 0;
+  *minor = 1;
+  *patch = 0;
+  return RF_OK;
+}
+
+int64_t rf_kernel_launch_count(void) { return g_launches.load(); }
+
+rf_status rf_sync_check(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string("stream sync: ") + cudaGetErrorString(e));
+  return take_device_error();
+}
+
+rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision, size_t* bytes) {
+  if (!bytes) return fail(RF_EINVAL, "null output pointer");
+  std::vector<LeafPlan> lp;
+  RF_TRY(leaves_from_abi(leaves, n_leaves, lp, false));
+  Plan P;
+  RF_TRY(build_plan(lp, precision, P));
+  *bytes = P.bytes;
+  return RF_OK;
+}
+
+rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!params) return fail(RF_EINVAL, "null params");
+  const rf_muon_params& p = *params;
+  if (!(p.beta >= 0.f && p.beta < 1.f)) return fail(RF_EINVAL, "beta must be in [0, 1)");
+  if (!(p.eps > 0.f)) return fail(RF_EINVAL, "eps must be positive");
+  if (p.accumulator != RF_EMA && p.accumulator != RF_HEAVY_BALL)
+    return fail(RF_EINVAL, "momentum_accumulator must be 'ema' or 'heavy_ball'");
+  if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
+  RF_TRY(check_coeffs(p.coeffs, p.n_coeff_rows, p.ns_steps));
+  std::vector<LeafPlan> lp;
+  RF_TRY(leaves_from_abi(leaves, n_leaves, lp, true));
+  Plan P;
+  RF_TRY(build_plan(lp, p.precision, P));
+  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, p.ns_steps, p.eps, p.fuse_tail, p.lr,
+                      workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
+                            void* stream) {
+  if (!params) return fail(RF_EINVAL, "null params");
+  const rf_muon_params& p = *params;
+  if (!(p.beta >= 0.f && p.beta < 1.f)) return fail(RF_EINVAL, "beta must be in [0, 1)");
+  if (p.accumulator != RF_EMA && p.accumulator != RF_HEAVY_BALL)
+    return fail(RF_EINVAL, "momentum_accumulator must be 'ema' or 'heavy_ball'");
+  if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  const MomentumCoeffs mc = momentum_coeffs(p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DirLaunch D{};
+  D.c = mc;
+  int64_t chunks = 0;
+  for (int i = 0; i < n_leaves; ++i) {
+    const rf_muon_leaf& l = leaves[i];
+    RF_TRY(validate_leaf(l, i, true));
+    if (l.skip_ns) continue;
+    if (l.out_dtype != RF_F32) return fail(RF_EINVAL, "direction output must be float32");
+    DirLeafDev& d = D.leaf[D.n++];
+    d.g = l.grad;
+    d.mu = l.mu;
+    d.out = static_cast<float*>(l.out);
+    d.n = l.batch * l.rows * l.cols;
+    d.chunk_begin = chunks;
+    d.gdt = l.grad_dtype;
+    chunks += ceil_div(d.n, kChunk);
+    if (D.n == kMaxLeavesPerLaunch) {
+      D.total_chunks = chunks;
+      RF_TRY(launch_direction(D, st));
+      D = DirLaunch{};
+      D.c = mc;
+      chunks = 0;
+    }
+  }
+  D.total_chunks = chunks;
+  if (D.n) RF_TRY(launch_direction(D, st));
+  return RF_OK;
+}
+
+static rf_status ns_plan(int64_t batch, int64_t rows, int64_t cols, int32_t precision, Plan& P, const void* x,
+                         int32_t x_dtype, void* out, int32_t out_dtype) {
+  if (batch <= 0 || rows <= 0 || cols <= 0) return fail(RF_EINVAL, "batch/rows/cols must be positive");
+  LeafPlan l{};
+  l.g = x;
+  l.mu = nullptr;
+  l.out = out;
+  l.batch = batch;
+  l.rows = rows;
+  l.cols = cols;
+  l.transposed = rows > cols;
+  l.m = std::min(rows, cols);
+  l.n = std::max(rows, cols);
+  l.gdt = x_dtype;
+  l.pdt = RF_F32;
+  l.odt = out_dtype;
+  l.shape_scale = 1.f;
+  l.decay = 0.f;
+  return build_plan({l}, precision, P);
+}
+
+rf_status rf_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols, int32_t precision,
+                                          size_t* bytes) {
+  if (!bytes) return fail(RF_EINVAL, "null output pointer");
+  Plan P;
+  RF_TRY(ns_plan(batch, rows, cols, precision, P, nullptr, RF_F32, nullptr, RF_F32));
+  *bytes = P.bytes;
+  return RF_OK;
+}
+
+rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t out_dtype, int64_t batch,
+                           int64_t rows, int64_t cols, const float* coeffs, int32_t n_coeff_rows, int32_t ns_steps,
+                           float eps, int32_t precision, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !out) return fail(RF_EINVAL, "x and out must be non-null");
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(RF_EINVAL, "bad dtype");
+  if (!(eps > 0.f)) return fail(RF_EINVAL, "eps must be positive");
+  RF_TRY(check_coeffs(coeffs, n_coeff_rows, ns_steps));
+  Plan P;
+  RF_TRY(ns_plan(batch, rows, cols, precision, P, x, x_dtype, out, out_dtype));
+  MomentumCoeffs mc{};
+  mc.mode = kDirIdentity;
+  return run_pipeline(P, mc, coeffs, n_coeff_rows, ns_steps, eps, 0, 0.f, workspace, workspace_bytes,
+                      static_cast<cudaStream_t>(stream));
+}
+
+rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, void* stream) {
+  if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
+    TailLaunch T{};
+    T.neg_lr = -lr;
+    int64_t chunks = 0;
+    for (int i = s; i < std::min(n_leaves, s + kMaxLeavesPerLaunch); ++i) {
+      const rf_tail_leaf& l = leaves[i];
+      if (l.n < 0 || (l.n > 0 && (!l.o || !l.out))) return fail(RF_EINVAL, "tail leaf " + std::to_string(i) + ": bad pointers");
+      if (!valid_dtype(l.o_dtype) || !valid_dtype(l.out_dtype)) return fail(RF_EINVAL, "tail leaf: bad dtype");
+      if (l.decay != 0.f && (!l.param || !valid_dtype(l.param_dtype)))
+        return fail(RF_EINVAL, "tail leaf: param required when decay != 0");
+      TailLeafDev& d = T.leaf[T.n++];
+      d.o = l.o;
+      d.p = l.param;
+      d.out = l.out;
+      d.n = l.n;
+      d.chunk_begin = chunks;
+      d.odt = l.o_dtype;
+      d.pdt = l.param ? l.param_dtype : RF_F32;
+      d.outdt = l.out_dtype;
+      d.shape_scale = l.shape_scale;
+      d.decay = l.decay;
+      chunks += ceil_div(l.n, kChunk);
+    }
+    T.total_chunks = chunks;
+    RF_TRY(launch_tail(T, st));
+  }
+  return RF_OK;
+}
+
+rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
+                          void* stream) {
+  if (!params) return fail(RF_EINVAL, "null params");
+  if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  const rf_adam_params& p = *params;
+  if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
+  AdamCoeffs c{};
+  const int t = p.count + 1;
+  c.b1 = p.b1;
+  c.b2 = p.b2;
+  c.one_minus_b1 = 1.0f - p.b1;                  // utils.py:333 (1 - decay32)
+  c.one_minus_b2 = float(1.0 - double(p.b2));     // utils.py:486 ((1.0 - decay) with a Python float)
+  c.one_minus_b1_py = float(1.0 - double(p.b1));  // adam.py:154 ((1.0 - b1) with a Python float)
+  c.bc1 = 1.0f - f32_pow(p.b1, t);                // adam.py:137
+  c.bc1_next = 1.0f - f32_pow(p.b1, t + 1);       // adam.py:141
+  c.bc2 = 1.0f - f32_pow(p.b2, t);                // adam.py:138
+  c.eps = p.eps;
+  c.eps_root = p.eps_root;
+  c.neg_lr = -p.lr;
+  c.nesterov = p.nesterov;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
+    AdamLaunch A{};
+    A.c = c;
+    int64_t chunks = 0;
+    for (int i = s; i < std::min(n_leaves, s + kMaxLeavesPerLaunch); ++i) {
+      const rf_adam_leaf& l = leaves[i];
+      if (l.n < 0 || (l.n > 0 && (!l.grad || !l.mu || !l.nu || !l.out)))
+        return fail(RF_EINVAL, "adam leaf " + std::to_string(i) + ": bad pointers");
+      if (!valid_dtype(l.grad_dtype) || !valid_dtype(l.out_dtype)) return fail(RF_EINVAL, "adam leaf: bad dtype");
+      if (l.decay != 0.f && (!l.param || !valid_dtype(l.param_dtype)))
+        return fail(RF_EINVAL, "adam leaf: param required when decay != 0");
+      AdamLeafDev& d = A.leaf[A.n++];
+      d.g = l.grad;
+      d.mu = l.mu;
+      d.nu = l.nu;
+      d.p = l.param;
+      d.out = l.out;
+      d.n = l.n;
+      d.chunk_begin = chunks;
+      d.gdt = l.grad_dtype;
+      d.pdt = l.param ? l.param_dtype : RF_F32;
+      d.odt = l.out_dtype;
+      d.decay = l.decay;
+      d.decay_dt = l.decay_rounding;
+      if (l.decay != 0.f && !valid_dtype(l.decay_rounding)) return fail(RF_EINVAL, "adam leaf: bad decay_rounding");
+      chunks += ceil_div(l.n, kChunk);
+    }
+    A.total_chunks = chunks;
+    RF_TRY(launch_adamw(A, st));
+  }
+  return RF_OK;
+}
+
+}  // extern "C"

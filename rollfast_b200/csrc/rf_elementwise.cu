@@ -1,0 +1,365 @@
+// HBM-bound kernels of the Muon step (sm_100a):
+//   k_momentum_sumsq   momentum update + Nesterov/bias-corrected direction,
+//                      per-chunk partial sums of direction^2     (utils.py:437-645)
+//   k_norm_finalize    per-matrix 1/(||d||_F + eps) from the partials
+//                      (orthogonalization.py:243-246)
+//   k_ns_load          direction -> scaled 16-bit (or fp32) NS operand, tiled
+//                      transpose for rows > cols, zero padding (orthogonalization.py:227-231)
+//   k_adamw            (N)AdamW fallback leaves (adam.py:123-177) + decay + LR
+//   k_tail             -lr * (shape_scale * O + decay * p)  (muon.py:79-139, 390-393, 466)
+//
+// All leaf tables travel as kernel parameters (large-parameter launches), so
+// every launch is self-contained and capturable in a CUDA graph.
+#include "rf_kernels.cuh"
+
+namespace rf {
+
+// ---------------------------------------------------------------------------
+// Direction formula (the reference's _prepare_first_moment_runtime with
+// bias_correction=True, nesterov_moment_count_offset=1).  All products and
+// sums are rounded separately (no FMA contraction) so `mu` matches the
+// reference's float32 arithmetic bit for bit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float momentum_new(const MomentumCoeffs& c, float g, float mu) {
+  return __fadd_rn(__fmul_rn(c.s, g), __fmul_rn(c.beta, mu));
+}
+
+__device__ __forceinline__ float direction(const MomentumCoeffs& c, float g, float mu_new) {
+  switch (c.mode) {
+    case kDirEmaNesterov:
+      return __fadd_rn(__fmul_rn(c.beta, __fdiv_rn(mu_new, c.bc_mu)),
+                       __fmul_rn(c.s, __fdiv_rn(g, c.bc_g)));
+    case kDirEma:
+      return __fdiv_rn(mu_new, c.bc_mu);
+    case kDirHeavyBallNesterov:
+      return __fadd_rn(__fmul_rn(c.beta, mu_new), __fmul_rn(c.s, g));
+    case kDirHeavyBall:
+      return mu_new;
+    default:  // kDirIdentity: plain NS input (orthogonalize_fn seam)
+      return g;
+  }
+}
+
+template <int GDT>
+struct GradVec;
+template <>
+struct GradVec<RF_F32> {
+  static __device__ __forceinline__ void load8(const void* p, int64_t i, float* v) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    float4 a = __ldcs(q), b = __ldcs(q + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+};
+template <>
+struct GradVec<RF_BF16> {
+  static __device__ __forceinline__ void load8(const void* p, int64_t i, float* v) {
+    uint4 raw = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + i));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = __bfloat1622float2(h[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  }
+};
+template <>
+struct GradVec<RF_F16> {
+  static __device__ __forceinline__ void load8(const void* p, int64_t i, float* v) {
+    uint4 raw = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + i));
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f = __half22float2(h[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  }
+};
+
+__device__ __forceinline__ int find_leaf(const int64_t* begins, int n, int64_t key) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (begins[mid] <= key) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = (l < int(blockDim.x >> 5)) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  return t;  // valid in thread 0
+}
+
+// ---------------------------------------------------------------------------
+// k_momentum_sumsq: one CTA per chunk of kChunk elements of one matrix.
+// ---------------------------------------------------------------------------
+template <int GDT>
+__global__ void __launch_bounds__(kEwThreads) k_momentum_sumsq(const __grid_constant__ MomentumLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  __shared__ float red[32];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, chunk);
+    const MomentumLeaf& L = P.leaf[li];
+    const int64_t local = chunk - L.chunk_begin;
+    const int64_t mat = local / L.chunks_per_mat;
+    const int64_t cim = local - mat * L.chunks_per_mat;
+    const int64_t base = mat * L.numel;
+    const int64_t lo = cim * kChunk;
+    const int64_t hi = (lo + kChunk < L.numel ? lo + kChunk : L.numel);
+    float acc = 0.f;
+    if (L.vec_ok) {
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float g[8], m[8];
+        GradVec<GDT>::load8(L.g, base + i, g);
+        float4* mp = reinterpret_cast<float4*>(L.mu + base + i);
+        float4 m0 = mp[0], m1 = mp[1];
+        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
+        m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          m[k] = momentum_new(P.c, g[k], m[k]);
+          const float d = direction(P.c, g[k], m[k]);
+          acc = fmaf(d, d, acc);
+        }
+        mp[0] = make_float4(m[0], m[1], m[2], m[3]);
+        mp[1] = make_float4(m[4], m[5], m[6], m[7]);
+      }
+    } else {
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float g = ld_as_float(L.g, GDT, base + i);
+        float m = L.mu ? L.mu[base + i] : 0.f;
+        if (L.mu) {
+          m = momentum_new(P.c, g, m);
+          L.mu[base + i] = m;
+        }
+        const float d = direction(P.c, g, m);
+        acc = fmaf(d, d, acc);
+      }
+    }
+    const float t = block_sum(acc, red);
+    if (threadIdx.x == 0) P.partials[chunk] = t;
+  }
+}
+
+// Plain sum of squares (orthogonalize_fn seam, no momentum): same kernel with
+// mu == nullptr and kDirIdentity.
+
+// ---------------------------------------------------------------------------
+// k_norm_finalize: one CTA per matrix, fixed-order reduction of its partials.
+// denom[mat] = ||d||_F + eps (orthogonalization.py:244-246).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kEwThreads) k_norm_finalize(const __grid_constant__ MomentumLaunch P,
+                                                              float* __restrict__ denom_out, float eps) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  __shared__ float red[32];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].mat_begin;
+  __syncthreads();
+  for (int64_t mat = blockIdx.x; mat < P.total_mats; mat += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, mat);
+    const MomentumLeaf& L = P.leaf[li];
+    const int64_t local_mat = mat - L.mat_begin;
+    const int64_t c0 = L.chunk_begin + local_mat * L.chunks_per_mat;
+    float acc = 0.f;
+    for (int64_t i = threadIdx.x; i < L.chunks_per_mat; i += blockDim.x) acc += P.partials[c0 + i];
+    const float t = block_sum(acc, red);
+    if (threadIdx.x == 0) {
+      denom_out[L.scale_index + local_mat] = __fadd_rn(__fsqrt_rn(t), eps);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_ns_load: builds the padded NS operand X~0 = round(sx * (d / (||d|| + eps)))
+// for every matrix of one shape group.  64x64 output tiles; a transposed leaf
+// (rows > cols) is read along its rows and written along the NS rows through
+// shared memory, so both sides stay coalesced.
+// ---------------------------------------------------------------------------
+template <typename OT>
+__global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLaunch P) {
+  __shared__ float tile[64][65];
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].group_mat_begin;
+  __syncthreads();
+  const int64_t tiles_r = P.mp / 64, tiles_c = P.np / 64;
+  const int64_t tiles_per_mat = tiles_r * tiles_c;
+  const int64_t total = tiles_per_mat * P.group_mats;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t gm = t / tiles_per_mat;
+    const int64_t tl = t - gm * tiles_per_mat;
+    const int64_t r0 = (tl / tiles_c) * 64, c0 = (tl % tiles_c) * 64;
+    const int li = find_leaf(s_begin, P.n, gm);
+    const LoadLeaf& L = P.leaf[li];
+    const int64_t bi = gm - L.group_mat_begin;
+    const int64_t numel = L.rows * L.cols;
+    const int64_t base = bi * numel;
+    const float denom = P.denom[L.norm_index + bi];
+    // Input tile: rows ir0.., cols ic0.. of the leaf matrix (rows x cols).
+    const int64_t ir0 = L.transposed ? c0 : r0;
+    const int64_t ic0 = L.transposed ? r0 : c0;
+    __syncthreads();
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+      const int ii = e >> 6, jj = e & 63;
+      const int64_t ir = ir0 + ii, ic = ic0 + jj;
+      float v = 0.f;
+      if (ir < L.rows && ic < L.cols) {
+        const int64_t idx = base + ir * L.cols + ic;
+        const float g = ld_as_float(L.g, L.gdt, idx);
+        const float m = L.mu ? L.mu[idx] : 0.f;
+        // X / (||X|| + eps) as the reference divides, then the exact
+        // power-of-two operand scale.
+        v = __fmul_rn(__fdiv_rn(direction(P.c, g, m), denom), P.sx);
+      }
+      tile[ii][jj] = v;
+    }
+    __syncthreads();
+    OT* out = static_cast<OT*>(P.x) + gm * P.mp * P.np;
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+      const int ii = e >> 6, jj = e & 63;  // output (r0+ii, c0+jj)
+      const float v = L.transposed ? tile[jj][ii] : tile[ii][jj];
+      out[(r0 + ii) * P.np + (c0 + jj)] = from_float<OT>(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_adamw: multi-tensor (N)AdamW.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ AdamLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  const AdamCoeffs& c = P.c;
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, chunk);
+    const AdamLeafDev& L = P.leaf[li];
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float g = ld_as_float(L.g, L.gdt, i);
+      const float mu = __fadd_rn(__fmul_rn(c.one_minus_b1, g), __fmul_rn(c.b1, L.mu[i]));
+      const float nu = __fadd_rn(__fmul_rn(c.one_minus_b2, __fmul_rn(g, g)), __fmul_rn(c.b2, L.nu[i]));
+      L.mu[i] = mu;
+      L.nu[i] = nu;
+      float mh;
+      if (c.nesterov) {
+        mh = __fadd_rn(__fmul_rn(c.b1, __fdiv_rn(mu, c.bc1_next)),
+                       __fmul_rn(c.one_minus_b1_py, __fdiv_rn(g, c.bc1)));
+      } else {
+        mh = __fdiv_rn(mu, c.bc1);
+      }
+      const float nh = __fdiv_rn(nu, c.bc2);
+      float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(__fadd_rn(nh, c.eps_root)), c.eps));
+      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, ld_as_float(L.p, L.pdt, i)));
+      st_from_float(L.out, L.odt, i, __fmul_rn(c.neg_lr, u));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_direction: mu <- s g + beta mu; out <- direction (custom orthogonalize_fn).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kEwThreads) k_direction(const __grid_constant__ DirLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, chunk);
+    const DirLeafDev& L = P.leaf[li];
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float g = ld_as_float(L.g, L.gdt, i);
+      const float m = momentum_new(P.c, g, L.mu[i]);
+      L.mu[i] = m;
+      L.out[i] = direction(P.c, g, m);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k_tail: out = -lr * (shape_scale * O + decay * p) for gathered leaves.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kEwThreads) k_tail(const __grid_constant__ TailLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, chunk);
+    const TailLeafDev& L = P.leaf[li];
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      float u = __fmul_rn(ld_as_float(L.o, L.odt, i), L.shape_scale);
+      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.pdt, L.decay, ld_as_float(L.p, L.pdt, i)));
+      st_from_float(L.out, L.outdt, i, __fmul_rn(P.neg_lr, u));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers.
+// ---------------------------------------------------------------------------
+static int ew_grid(int64_t work) {
+  const int64_t cap = int64_t(num_sms()) * 8;
+  return int(work < cap ? (work > 0 ? work : 1) : cap);
+}
+
+rf_status launch_momentum_sumsq(const MomentumLaunch& P, int gdt, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  const int grid = ew_grid(P.total_chunks);
+  if (gdt == RF_F32) k_momentum_sumsq<RF_F32><<<grid, kEwThreads, 0, st>>>(P);
+  else if (gdt == RF_BF16) k_momentum_sumsq<RF_BF16><<<grid, kEwThreads, 0, st>>>(P);
+  else k_momentum_sumsq<RF_F16><<<grid, kEwThreads, 0, st>>>(P);
+  return check_launch("k_momentum_sumsq");
+}
+
+rf_status launch_norm_finalize(const MomentumLaunch& P, float* denom, float eps, cudaStream_t st) {
+  if (P.total_mats == 0) return RF_OK;
+  k_norm_finalize<<<ew_grid(P.total_mats), kEwThreads, 0, st>>>(P, denom, eps);
+  return check_launch("k_norm_finalize");
+}
+
+rf_status launch_ns_load(const LoadLaunch& P, int precision, cudaStream_t st) {
+  const int64_t total = (P.mp / 64) * (P.np / 64) * P.group_mats;
+  if (total == 0) return RF_OK;
+  const int grid = int(total < int64_t(num_sms()) * 16 ? total : int64_t(num_sms()) * 16);
+  if (precision == RF_NS_F16) k_ns_load<__half><<<grid, 256, 0, st>>>(P);
+  else if (precision == RF_NS_BF16) k_ns_load<__nv_bfloat16><<<grid, 256, 0, st>>>(P);
+  else k_ns_load<float><<<grid, 256, 0, st>>>(P);
+  return check_launch("k_ns_load");
+}
+
+rf_status launch_adamw(const AdamLaunch& P, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  k_adamw<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  return check_launch("k_adamw");
+}
+
+rf_status launch_direction(const DirLaunch& P, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  k_direction<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  return check_launch("k_direction");
+}
+
+rf_status launch_tail(const TailLaunch& P, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  k_tail<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  return check_launch("k_tail");
+}
+
+}  // namespace rf

@@ -1,0 +1,216 @@
+// Launch descriptors and launcher declarations shared by the kernels and the
+// C-ABI layer.  Leaf tables are passed by value as kernel parameters.
+#pragma once
+
+#include "rf_common.cuh"
+
+namespace rf {
+
+constexpr int kEwThreads = 256;
+constexpr int64_t kChunk = 8192;          // elements per CTA-chunk in multi-tensor kernels
+constexpr int kMaxLeavesPerLaunch = 64;   // leaf-table entries per launch
+
+int num_sms();
+
+enum DirMode : int {
+  kDirEmaNesterov = 0,
+  kDirEma = 1,
+  kDirHeavyBallNesterov = 2,
+  kDirHeavyBall = 3,
+  kDirIdentity = 4
+};
+
+struct MomentumCoeffs {
+  float s;      // 1 - beta (ema) or 1 (heavy ball), utils.py:327-339
+  float beta;
+  float bc_mu;  // 1 - beta^(t+1) under Nesterov, else 1 - beta^t (ema only)
+  float bc_g;   // 1 - beta^t (ema + Nesterov only)
+  int mode;     // DirMode
+};
+
+struct MomentumLeaf {
+  const void* g;
+  float* mu;             // nullptr in kDirIdentity mode
+  int64_t numel;         // elements per matrix (rows * cols)
+  int64_t chunk_begin;   // first global chunk of this leaf
+  int64_t mat_begin;     // first matrix index (within this launch) of this leaf
+  int64_t scale_index;   // index of its first matrix in the per-matrix scale array
+  int32_t chunks_per_mat;
+  int32_t vec_ok;        // 16-byte aligned and numel % 8 == 0
+};
+
+struct MomentumLaunch {
+  MomentumLeaf leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  int64_t total_mats;
+  float* partials;         // [total_chunks] for this launch
+  MomentumCoeffs c;
+};
+
+struct LoadLeaf {
+  const void* g;
+  const float* mu;
+  int64_t rows, cols;        // leaf matrix (before the NS transpose)
+  int64_t group_mat_begin;   // first matrix of this leaf within the group
+  int64_t norm_index;        // index of its first matrix in the denominator array
+  int32_t transposed;
+  int32_t gdt;
+};
+
+struct LoadLaunch {
+  LoadLeaf leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t group_mats;  // matrices covered by this launch
+  int64_t mp, np;      // padded NS dims
+  const float* denom;  // per-matrix ||d||_F + eps
+  float sx;            // power-of-two operand scale of this group
+  void* x;             // X~0 for matrix 0 of this launch
+  MomentumCoeffs c;
+};
+
+struct AdamCoeffs {
+  float b1, b2, one_minus_b1, one_minus_b2, one_minus_b1_py;
+  float bc1, bc1_next, bc2, eps, eps_root, neg_lr;
+  int nesterov;
+};
+struct AdamLeafDev {
+  const void* g;
+  float* mu;
+  float* nu;
+  const void* p;
+  void* out;
+  int64_t n, chunk_begin;
+  int32_t gdt, pdt, odt, decay_dt;
+  float decay;
+};
+struct AdamLaunch {
+  AdamLeafDev leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  AdamCoeffs c;
+};
+
+struct DirLeafDev {
+  const void* g;
+  float* mu;
+  float* out;
+  int64_t n, chunk_begin;
+  int32_t gdt;
+};
+struct DirLaunch {
+  DirLeafDev leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  MomentumCoeffs c;
+};
+
+struct TailLeafDev {
+  const void* o;
+  const void* p;
+  void* out;
+  int64_t n, chunk_begin;
+  int32_t odt, pdt, outdt;
+  float shape_scale, decay;
+};
+struct TailLaunch {
+  TailLeafDev leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  float neg_lr;
+};
+
+// --- Newton-Schulz GEMM stages ------------------------------------------------
+// One call runs one of the three products of an NS iteration for every
+// matrix of a shape group (padded to mp x np, multiples of 256):
+//   kSyrkXXt : A~  = round(alpha * X~ X~^T)                    (upper tiles, mirrored)
+//   kSyrkPoly: B~  = round(alpha * A~ A~ + beta * A~)          (upper tiles, mirrored)
+//   kGemmBX  : X~' = round(alpha * B~ X~ + beta * X~)
+//   kGemmBXFinal: O = (alpha * B~ X~ + beta * X~) * out_scale, written to each
+//                 leaf in its own layout (transposed back when rows > cols),
+//                 optionally with the fused tail -lr * (shape * O + decay * p).
+enum NsStage : int { kSyrkXXt = 0, kSyrkPoly = 1, kGemmBX = 2, kGemmBXFinal = 3 };
+
+struct FinalLeaf {
+  void* out;
+  const void* p;
+  int64_t group_mat_begin;
+  int32_t transposed;
+  int32_t out_dtype, p_dtype;
+  float shape_scale, decay;
+};
+
+struct NsGemmArgs {
+  int stage;
+  int precision;       // rf_ns_precision (operand storage)
+  int64_t G;           // matrices in the group
+  int64_t m, n;        // true NS dims (m <= n)
+  int64_t mp, np;      // padded dims
+  const void* a_op;    // A operand [G][mp][K]  (X~ for XXt, A~ for Poly, B~ for BX)
+  const void* b_op;    // B operand (X~ for XXt, A~ for Poly, X~ [G][mp][np] for BX)
+  const void* aux;     // epilogue aux (A~ for Poly, X~ for BX)
+  void* out;           // A~ / B~ / X~' (not used by the final stage)
+  float alpha, beta;
+  // final stage
+  float out_scale;     // 1 / sx
+  int fuse_tail;
+  float neg_lr;
+  int n_final;
+  FinalLeaf final_leaf[kMaxLeavesPerLaunch];
+};
+
+rf_status launch_momentum_sumsq(const MomentumLaunch& P, int gdt, cudaStream_t st);
+rf_status launch_norm_finalize(const MomentumLaunch& P, float* denom, float eps, cudaStream_t st);
+rf_status launch_ns_load(const LoadLaunch& P, int precision, cudaStream_t st);
+rf_status launch_adamw(const AdamLaunch& P, cudaStream_t st);
+rf_status launch_tail(const TailLaunch& P, cudaStream_t st);
+rf_status launch_direction(const DirLaunch& P, cudaStream_t st);
+
+// NS GEMM stage: tcgen05 path for 16-bit operands, SIMT path for fp32 (or
+// when forced for cross-checking).
+rf_status launch_ns_gemm(const NsGemmArgs& a, cudaStream_t st);
+rf_status launch_ns_gemm_simt(const NsGemmArgs& a, cudaStream_t st);
+rf_status launch_ns_gemm_tc(const NsGemmArgs& a, cudaStream_t st);
+
+template <typename T>
+__device__ __forceinline__ T from_float(float v);
+template <>
+__device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename T>
+__device__ __forceinline__ float to_float(T v);
+template <>
+__device__ __forceinline__ float to_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_float<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Shared final-stage epilogue for one element (r, c) of matrix gm.
+__device__ __forceinline__ int find_final_leaf(const NsGemmArgs& a, int64_t gm) {
+  int lo = 0, hi = a.n_final - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (a.final_leaf[mid].group_mat_begin <= gm) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf& L, int64_t bi, int64_t r,
+                                            int64_t c, float o) {
+  // Leaf matrix is (m x n) when not transposed, (n x m) when transposed.
+  const int64_t idx = bi * a.m * a.n + (L.transposed ? c * a.m + r : r * a.n + c);
+  float v = o;
+  if (a.fuse_tail) {
+    v = __fmul_rn(o, L.shape_scale);
+    if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.p_dtype, L.decay, ld_as_float(L.p, L.p_dtype, idx)));
+    v = __fmul_rn(a.neg_lr, v);
+  }
+  st_from_float(L.out, L.out_dtype, idx, v);
+}
+
+}  // namespace rf

@@ -1,0 +1,227 @@
+"""Multi-GPU Muon: FLOP-balanced leaf ownership + all-gather of the
+orthogonalised leaves.
+
+One process per GPU.  Every rank holds the (data-parallel, already reduced)
+gradients of all leaves.  The Muon leaves are assigned to ranks by
+longest-processing-time-first on their Newton-Schulz FLOPs
+(4 m^2 n + 2 m^3 per matrix per iteration, m <= n); each rank runs the
+momentum + Newton-Schulz pipeline for its own leaves only, writing O in the
+leaf layout into its segment of a packed buffer, and an NCCL all-gather over
+NVLink returns every rank's segments.  Buckets of leaves are gathered on a
+side stream while the next bucket's Newton-Schulz runs.  Every rank then
+applies the tail -lr (shape * O + decay * p) to all leaves.
+
+Momentum for a leaf is kept current only on the rank that owns it; the
+ownership plan is deterministic for a given leaf list and world size.
+
+The reference has no collective on this path (its Muon runs every leaf on
+every device); ownership + all-gather is the B200 scaling design.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Callable, Sequence
+
+import torch
+
+from . import _lib, _runtime
+
+_ctx = None
+
+
+@dataclass
+class ShardContext:
+    rank: int
+    world_size: int
+    group: object = None
+    buckets: int = 4
+    plans: dict = field(default_factory=dict)
+    comm_stream: object = None
+
+
+def configure(group=None, *, buckets: int = 4) -> ShardContext:
+    """Enable sharded Muon updates over ``group`` (default: the world group)."""
+    import torch.distributed as dist
+
+    global _ctx
+    if not dist.is_initialized():
+        raise RuntimeError("torch.distributed must be initialised before rollfast_b200.distributed.configure")
+    _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
+                        buckets=max(1, int(buckets)))
+    return _ctx
+
+
+def current() -> ShardContext | None:
+    return _ctx
+
+
+def clear() -> None:
+    global _ctx
+    _ctx = None
+
+
+# ---------------------------------------------------------------------------
+# Planning (pure host logic; exercised by CPU tests)
+# ---------------------------------------------------------------------------
+
+
+def ns_flops(batch: int, rows: int, cols: int) -> int:
+    """Dense NS FLOPs per iteration for a (batch, rows, cols) leaf."""
+    m, n = min(rows, cols), max(rows, cols)
+    return batch * (4 * m * m * n + 2 * m * m * m)
+
+
+def lpt_assign(costs: Sequence[int], world_size: int) -> list[int]:
+    """Longest-processing-time-first: leaves in decreasing cost order go to
+    the currently least-loaded rank (ties: lowest rank, then input order)."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    load = [0] * world_size
+    owner = [0] * len(costs)
+    for i in order:
+        r = min(range(world_size), key=lambda k: (load[k], k))
+        owner[i] = r
+        load[r] += costs[i]
+    return owner
+
+
+@dataclass
+class BucketPlan:
+    leaves: list[int]                 # global leaf indices in this bucket
+    seg: int                          # per-rank segment length (elements)
+    offsets: dict                     # leaf -> (owner, offset within owner's segment)
+
+
+@dataclass
+class ShardPlan:
+    owner: list[int]
+    buckets: list[BucketPlan]
+    loads: list[int]
+
+
+def make_plan(sizes: Sequence[int], costs: Sequence[int], world_size: int, n_buckets: int) -> ShardPlan:
+    """Ownership + bucket layout.  Buckets split the leaf list (in order) into
+    ``n_buckets`` runs of roughly equal total cost, the last one smallest so
+    the exposed final all-gather is short."""
+    owner = lpt_assign(costs, world_size)
+    n = len(sizes)
+    total = sum(costs) or 1
+    # Cost targets decreasing geometrically towards the end.
+    weights = [2.0 ** (n_buckets - 1 - k) for k in range(n_buckets)]
+    wsum = sum(weights)
+    bounds, acc, k = [], 0.0, 0
+    target = weights[0] / wsum * total
+    start = 0
+    for i in range(n):
+        acc += costs[i]
+        if acc >= target and k < n_buckets - 1 and i + 1 < n:
+            bounds.append((start, i + 1))
+            start = i + 1
+            k += 1
+            target += weights[k] / wsum * total
+    bounds.append((start, n))
+    buckets = []
+    for lo, hi in bounds:
+        if lo >= hi:
+            continue
+        used = [0] * world_size
+        offsets = {}
+        for i in range(lo, hi):
+            r = owner[i]
+            offsets[i] = (r, used[r])
+            used[r] += sizes[i]
+        buckets.append(BucketPlan(list(range(lo, hi)), max(used) if used else 0, offsets))
+    loads = [0] * world_size
+    for i, r in enumerate(owner):
+        loads[r] += costs[i]
+    return ShardPlan(owner, buckets, loads)
+
+
+def exchange_bucket(bucket: BucketPlan, rank: int, world_size: int, send: torch.Tensor, group,
+                    all_gather: Callable | None = None) -> torch.Tensor:
+    """All-gather one bucket's per-rank segments: returns [world * seg]."""
+    import torch.distributed as dist
+
+    recv = torch.empty(world_size * bucket.seg, dtype=send.dtype, device=send.device)
+    if all_gather is None:
+        dist.all_gather_into_tensor(recv, send, group=group)
+    else:
+        all_gather(recv, send)
+    return recv
+
+
+def leaf_view(bucket: BucketPlan, recv: torch.Tensor, leaf: int, numel: int) -> torch.Tensor:
+    r, off = bucket.offsets[leaf]
+    base = r * bucket.seg + off
+    return recv[base:base + numel]
+
+
+# ---------------------------------------------------------------------------
+# GPU path
+# ---------------------------------------------------------------------------
+
+_O_DTYPE = {_lib.RF_NS_F16: torch.float16, _lib.RF_NS_BF16: torch.bfloat16, _lib.RF_NS_F32: torch.float32}
+
+
+def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float):
+    """Sharded version of the fused Muon-branch update (see module doc)."""
+    from .base import rf_dtype, run_tail, stream_handle
+    from .muon import _leaf_table
+
+    if not ml:
+        return []
+    dev = ml[0].g.device
+    sizes = [L.out.numel() for L in ml]
+    key = tuple((L.layout.flat_shape, L.g.dtype) for L in ml)
+    plan = ctx.plans.get(key)
+    if plan is None:
+        steps = prm.ns_steps
+        costs = [ns_flops(*L.layout.flat_shape) * steps for L in ml]
+        plan = make_plan(sizes, costs, ctx.world_size, ctx.buckets)
+        ctx.plans[key] = plan
+    odt = _O_DTYPE[prm.precision]
+    lib = _lib.load()
+    compute = torch.cuda.current_stream(dev)
+    if ctx.comm_stream is None:
+        ctx.comm_stream = torch.cuda.Stream(device=dev)
+    comm = ctx.comm_stream
+    prm.fuse_tail = 0
+    recvs = []
+    for b in plan.buckets:
+        send = torch.empty(max(b.seg, 1), dtype=odt, device=dev)
+        mine = [i for i in b.leaves if plan.owner[i] == ctx.rank]
+        if mine:
+            sub = [ml[i] for i in mine]
+            arr = _leaf_table(sub, [1.0] * len(sub), [0.0] * len(sub))
+            for j, i in enumerate(mine):
+                off = b.offsets[i][1]
+                arr[j].out = send.data_ptr() + off * send.element_size()
+                arr[j].out_dtype = rf_dtype(send)
+            nbytes = ctypes.c_size_t()
+            _lib.check(lib.rf_muon_workspace_size(arr, len(sub), prm.precision, ctypes.byref(nbytes)))
+            ws = _runtime.workspace(dev, nbytes.value)
+            _lib.check(lib.rf_muon_update(arr, len(sub), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
+                                          stream_handle(ml[0].g)))
+        ready = torch.cuda.Event()
+        ready.record(compute)
+        comm.wait_event(ready)
+        with torch.cuda.stream(comm):
+            recv = exchange_bucket(b, ctx.rank, ctx.world_size, send[: b.seg] if b.seg else send[:0], ctx.group)
+            send.record_stream(comm)
+            recv.record_stream(comm)
+        recvs.append(recv)
+    done = torch.cuda.Event()
+    done.record(comm)
+    compute.wait_event(done)
+    items = []
+    for b, recv in zip(plan.buckets, recvs):
+        for i in b.leaves:
+            L = ml[i]
+            o = leaf_view(b, recv, i, sizes[i])
+            p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+            items.append((o, p, L.out.view(-1), scales[i], decays[i]))
+    run_tail(items, lr)
+    from .muon import _finish_leaves
+
+    return _finish_leaves(ml)

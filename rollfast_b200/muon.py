@@ -1,0 +1,500 @@
+"""Muon (restates src/rollfast/optim/muon.py) on the B200 kernels.
+
+``muon(...)`` keeps the reference signature and state layout
+(``partition({"muon": chain(chain(scale_by_muon, scale_by_shape,
+[add_decayed_weights]), scale_by_learning_rate), "adam": adamw(...)})``,
+muon.py:398-486).  Its update runs the whole Muon branch as one
+``rf_muon_update`` call (momentum, Frobenius normalisation, grouped
+Newton-Schulz on tcgen05, shape scale, decay and learning rate fused into
+the last GEMM's epilogue) and the fallback leaves as one ``rf_adamw_update``
+call.  State buffers are updated in place (the equivalent of JAX buffer
+donation); the returned state holds the same tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Any, NamedTuple
+
+import torch
+
+from . import _lib, _runtime
+from .adam import ScaleByAdamState, adamw, fresh_key, run_adam, zeros_like_tree
+from .base import (
+    AddDecayedWeightsState,
+    EmptyState,
+    GradientTransformation,
+    MaskedState,
+    PartitionState,
+    ScaleByScheduleState,
+    ScaleState,
+    add_decayed_weights,
+    chain,
+    has_nonzero_or_scheduled,
+    host_count,
+    init_empty_state,
+    new_count,
+    partition,
+    resolve_mask,
+    resolve_scalar,
+    rf_dtype,
+    require_cuda,
+    round_to_dtype,
+    run_tail,
+    safe_increment,
+    scale_by_learning_rate,
+    stream_handle,
+    validate_beta,
+    validate_positive,
+)
+from .dimension_numbers import (
+    MatrixDimensionNumbers,
+    MuonDimensionNumbers,
+    _compute_matrix_layout,
+    _is_dimension_numbers_leaf,
+    _make_matrix_partition_fns,
+    _normalize_axes,
+    _resolve_update_dimension_numbers,
+    _validate_matrix_operand,
+)
+from .orthogonalization import (
+    MUON_NS_COEFFS,
+    coeff_buffer,
+    orthogonalize_via_newton_schulz,
+    polar_express_coeffs,
+    resolve_ns_coeffs,
+)
+from .tree import MaskedNode, is_aux_leaf, tree_flatten, tree_unflatten
+
+_DEFAULT_NS_COEFFS = MUON_NS_COEFFS
+
+
+class MuonState(NamedTuple):
+    """muon.py:60-67."""
+
+    count: torch.Tensor
+    mu: Any
+    ns_coeffs: torch.Tensor
+    magma_s: Any
+    key: Any
+
+
+# ---------------------------------------------------------------------------
+# Shape factors (muon.py:70-120)
+# ---------------------------------------------------------------------------
+
+
+def _get_shape_products(shape, dim_nums: MatrixDimensionNumbers) -> tuple[int, int]:
+    """muon.py:70-76."""
+    red, out = _normalize_axes(shape, dim_nums)
+    return math.prod(shape[a] for a in red), math.prod(shape[a] for a in out)
+
+
+def shape_factor(shape, dim_nums, consistent_rms=None) -> float:
+    """muon.py:79-100 as a float32 scalar: sqrt(max(1, fan_out/fan_in)) or
+    sqrt(max(fan_in, fan_out)) * consistent_rms."""
+    fan_in, fan_out = _get_shape_products(tuple(shape), dim_nums)
+    if consistent_rms is None:
+        v = torch.sqrt(torch.tensor(max(1.0, fan_out / fan_in), dtype=torch.float32))
+        return float(v)
+    v = torch.sqrt(torch.tensor(float(max(fan_in, fan_out)), dtype=torch.float32)) * torch.tensor(
+        float(consistent_rms), dtype=torch.float32)
+    return float(v)
+
+
+# ---------------------------------------------------------------------------
+# Leaf gathering
+# ---------------------------------------------------------------------------
+
+
+def _flatten_specs(dim_nums, n: int):
+    if isinstance(dim_nums, MatrixDimensionNumbers):
+        return [dim_nums]
+    specs = tree_flatten(dim_nums, is_leaf=_is_dimension_numbers_leaf)[0]
+    if len(specs) != n:
+        raise ValueError("weight_dimension_numbers tree does not match the update tree")
+    return specs
+
+
+class _MuonLeaf(NamedTuple):
+    pos: int
+    g: torch.Tensor       # (batch, R, O) view / copy
+    mu: torch.Tensor      # (batch, R, O) view / copy of the state buffer
+    mu_state: torch.Tensor
+    p: torch.Tensor | None
+    out: torch.Tensor     # (batch, R, O)
+    layout: Any
+    shape: tuple
+    spec: MatrixDimensionNumbers
+
+
+def _as_matrix(t: torch.Tensor, lay) -> torch.Tensor:
+    if lay.is_identity:
+        return t.contiguous().view(lay.flat_shape)
+    return t.permute(lay.perm).contiguous().view(lay.flat_shape)
+
+
+def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str):
+    out = []
+    for i, (g, spec) in enumerate(zip(leaves, specs)):
+        if is_aux_leaf(g):
+            continue
+        _validate_matrix_operand(g, spec, transform_name)
+        require_cuda(g, "gradient")
+        lay = _compute_matrix_layout(g.shape, g.dtype, spec)
+        mu_state = mus[i]
+        p = ps[i] if ps is not None else None
+        if p is not None and is_aux_leaf(p):
+            p = None
+        out.append(_MuonLeaf(
+            pos=i,
+            g=_as_matrix(g, lay),
+            mu=mu_state.view(lay.flat_shape) if lay.is_identity else _as_matrix(mu_state, lay),
+            mu_state=mu_state,
+            p=None if p is None else _as_matrix(p, lay),
+            out=torch.empty(lay.flat_shape, dtype=torch.float32, device=g.device),
+            layout=lay,
+            shape=tuple(g.shape),
+            spec=spec,
+        ))
+    return out
+
+
+def _leaf_table(ml: list, scales, decays):
+    arr = (_lib.RfMuonLeaf * max(1, len(ml)))()
+    for i, L in enumerate(ml):
+        b, r, c = L.layout.flat_shape
+        e = arr[i]
+        e.grad = L.g.data_ptr()
+        e.mu = L.mu.data_ptr()
+        e.param = L.p.data_ptr() if (L.p is not None and decays[i] != 0.0) else None
+        e.out = L.out.data_ptr()
+        e.batch, e.rows, e.cols = b, r, c
+        e.grad_dtype = rf_dtype(L.g)
+        e.param_dtype = rf_dtype(L.p) if L.p is not None else _lib.RF_F32
+        e.out_dtype = _lib.RF_F32
+        e.shape_scale = scales[i]
+        e.decay = decays[i]
+        e.skip_ns = 0
+    return arr
+
+
+def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail):
+    cbuf, rows = coeff_buffer(ns_coeffs)
+    if rows > 1 and rows < int(ns_steps):
+        raise ValueError(f"Not enough coeffs to perform {ns_steps} steps")
+    prm = _lib.RfMuonParams()
+    prm.beta = float(beta)
+    prm.eps = float(eps)
+    prm.count = int(count)
+    prm.nesterov = int(bool(nesterov))
+    prm.accumulator = _lib.RF_EMA if accumulator == "ema" else _lib.RF_HEAVY_BALL
+    prm.ns_steps = int(ns_steps)
+    prm.n_coeff_rows = rows
+    prm.coeffs = ctypes.cast(cbuf, ctypes.POINTER(ctypes.c_float))
+    prm.precision = _runtime.ns_precision()
+    prm.lr = float(lr)
+    prm.fuse_tail = int(fuse_tail)
+    return prm, cbuf
+
+
+def _run_muon_update(ml, prm, cbuf, scales, decays):
+    if not ml:
+        return
+    lib = _lib.load()
+    arr = _leaf_table(ml, scales, decays)
+    nbytes = ctypes.c_size_t()
+    _lib.check(lib.rf_muon_workspace_size(arr, len(ml), prm.precision, ctypes.byref(nbytes)))
+    dev = ml[0].g.device
+    ws = _runtime.workspace(dev, nbytes.value)
+    _lib.check(lib.rf_muon_update(arr, len(ml), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
+                                  stream_handle(ml[0].g)))
+    del cbuf
+
+
+def _finish_leaves(ml):
+    """Copy permuted momentum back and return outputs in leaf layout."""
+    outs = []
+    for L in ml:
+        if not L.layout.is_identity:
+            L.mu_state.copy_(L.mu.view(L.layout.unflat_shape).permute(L.layout.inv_perm))
+            outs.append(L.out.view(L.layout.unflat_shape).permute(L.layout.inv_perm).contiguous())
+        else:
+            outs.append(L.out.view(L.shape))
+    return outs
+
+
+def _validate_accumulator(acc: str) -> None:
+    if acc not in ("ema", "heavy_ball"):
+        raise ValueError(f"momentum_accumulator must be 'ema' or 'heavy_ball', got {acc!r}.")
+
+
+# ---------------------------------------------------------------------------
+# Transforms
+# ---------------------------------------------------------------------------
+
+
+def scale_by_muon_shape(weight_dimension_numbers=None, consistent_rms=None) -> GradientTransformation:
+    """muon.py:123-139."""
+    validate_positive("consistent_rms", consistent_rms)
+
+    def update_fn(updates, state, params=None):
+        dim_nums = _resolve_update_dimension_numbers(weight_dimension_numbers, params=params, updates=updates,
+                                                     transform_name="scale_by_muon_shape")
+        leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
+        specs = _flatten_specs(dim_nums, len(leaves))
+        items, outs = [], []
+        for u, d in zip(leaves, specs):
+            if is_aux_leaf(u) or d is None or isinstance(d, MaskedNode):
+                outs.append(u)
+                continue
+            require_cuda(u, "update")
+            o = torch.empty_like(u)
+            items.append((u.contiguous(), None, o, shape_factor(u.shape, d, consistent_rms), 0.0))
+            outs.append(o)
+        run_tail(items, -1.0)
+        return tree_unflatten(treedef, outs), state
+
+    return GradientTransformation(init_empty_state, update_fn)
+
+
+scale_by_shape = scale_by_muon_shape
+_resolve_ns_coeffs = resolve_ns_coeffs
+
+
+def _check_supported(*, adaptive, preconditioning, use_magma, mu_dtype, orthogonalize_fn):
+    if use_magma:
+        raise NotImplementedError("Magma masking is not on the B200 hot path")
+    if adaptive:
+        raise NotImplementedError("adaptive=True is not on the B200 hot path")
+    if mu_dtype is not None and mu_dtype not in (torch.float32, "float32", "f32"):
+        raise NotImplementedError("mu_dtype other than float32 (stochastic-rounding bf16 state) is not supported")
+    if preconditioning not in ("frobenius", "spectral", "aol", "schatten"):
+        raise ValueError(f"Unknown preconditioning {preconditioning!r}.")
+    if preconditioning != "frobenius" and orthogonalize_fn is orthogonalize_via_newton_schulz:
+        raise NotImplementedError(f"preconditioning={preconditioning!r} is not on the B200 hot path")
+
+
+def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8, mu_dtype=None, *,
+                  nesterov: bool = True, adaptive: bool = False, preconditioning: str = "frobenius",
+                  weight_dimension_numbers=None, orthogonalize_fn=orthogonalize_via_newton_schulz,
+                  momentum_accumulator: str = "ema", use_magma: bool = False, magma_p: float = 0.5,
+                  magma_tau: float = 2.0, shape_updates: bool = False, consistent_rms=None,
+                  weight_decay=0.0, weight_decay_mask=None, axis_name=None, key=None) -> GradientTransformation:
+    """muon.py:163-332: momentum + Nesterov + bias correction, then the
+    orthogonalisation hook (default: Newton-Schulz on the GPU)."""
+    if isinstance(ns_steps, (int, float)) and ns_steps < 1:
+        raise ValueError(f"ns_steps must be >= 1, got {ns_steps!r}.")
+    validate_beta("beta", beta)
+    validate_positive("eps", eps)
+    if shape_updates:
+        validate_positive("consistent_rms", consistent_rms)
+    if not use_magma and has_nonzero_or_scheduled(weight_decay):
+        raise ValueError(
+            "`weight_decay` in `scale_by_muon` is only applied by the Magma path. "
+            "Use `use_magma=True` or chain `optax.add_decayed_weights` separately."
+        )
+    _validate_accumulator(momentum_accumulator)
+    _check_supported(adaptive=adaptive, preconditioning=preconditioning, use_magma=use_magma, mu_dtype=mu_dtype,
+                     orthogonalize_fn=orthogonalize_fn)
+
+    def init_fn(params):
+        return MuonState(new_count(0), zeros_like_tree(params), resolve_ns_coeffs(ns_coeffs, ns_steps), (),
+                         fresh_key(key))
+
+    def update_fn(updates, state, params=None):
+        dim_nums = _resolve_update_dimension_numbers(weight_dimension_numbers, params=params, updates=updates,
+                                                     transform_name="scale_by_muon")
+        leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
+        specs = _flatten_specs(dim_nums, len(leaves))
+        for u, d in zip(leaves, specs):
+            _validate_matrix_operand(u, d, "scale_by_muon")
+        mus = tree_flatten(state.mu, is_leaf=is_aux_leaf)[0]
+        count = host_count(state.count)
+        ml = _gather_muon_leaves(leaves, mus, None, specs, "scale_by_muon")
+        prm, cbuf = _muon_params(beta=beta, eps=eps, count=count, nesterov=nesterov,
+                                 accumulator=momentum_accumulator, ns_coeffs=state.ns_coeffs, ns_steps=ns_steps,
+                                 lr=0.0, fuse_tail=0)
+        ones, zeros = [1.0] * len(ml), [0.0] * len(ml)
+        if orthogonalize_fn is orthogonalize_via_newton_schulz:
+            _run_muon_update(ml, prm, cbuf, ones, zeros)
+            outs = _finish_leaves(ml)
+        else:
+            # Caller-supplied hook: materialise the direction (mu_hat), then
+            # call the hook per leaf exactly as muon.py:258-271 does.
+            if ml:
+                arr = _leaf_table(ml, ones, zeros)
+                _lib.check(_lib.load().rf_muon_direction(arr, len(ml), ctypes.byref(prm), stream_handle(ml[0].g)))
+            dirs = _finish_leaves(ml)
+            outs = [orthogonalize_fn(d, state.ns_coeffs, ns_steps, preconditioning, eps, L.spec)
+                    for d, L in zip(dirs, ml)]
+        full = list(leaves)
+        for L, o in zip(ml, outs):
+            full[L.pos] = o
+        new_state = MuonState(safe_increment(state.count), state.mu, state.ns_coeffs, state.magma_s, state.key)
+        return tree_unflatten(treedef, full), new_state
+
+    return GradientTransformation(init_fn, update_fn)
+
+
+def _build_unscaled_muon_branch(*, ns_coeffs, ns_steps, beta, eps, mu_dtype, nesterov, adaptive, preconditioning,
+                                weight_dimension_numbers, orthogonalize_fn, momentum_accumulator, use_magma,
+                                magma_p, magma_tau, consistent_rms, weight_decay, weight_decay_mask, axis_name,
+                                key) -> GradientTransformation:
+    """muon.py:335-395."""
+    components = [
+        scale_by_muon(ns_coeffs=ns_coeffs, ns_steps=ns_steps, beta=beta, eps=eps, mu_dtype=mu_dtype,
+                      nesterov=nesterov, adaptive=adaptive, preconditioning=preconditioning,
+                      weight_dimension_numbers=weight_dimension_numbers, orthogonalize_fn=orthogonalize_fn,
+                      momentum_accumulator=momentum_accumulator, use_magma=use_magma, magma_p=magma_p,
+                      magma_tau=magma_tau, shape_updates=use_magma, consistent_rms=consistent_rms,
+                      weight_decay=weight_decay if use_magma else 0.0,
+                      weight_decay_mask=weight_decay_mask if use_magma else None, axis_name=axis_name, key=key)
+    ]
+    if not use_magma:
+        components.append(scale_by_shape(weight_dimension_numbers=weight_dimension_numbers,
+                                         consistent_rms=consistent_rms))
+        if has_nonzero_or_scheduled(weight_decay):
+            components.append(add_decayed_weights(weight_decay, weight_decay_mask))
+    return chain(*components)
+
+
+def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8, weight_decay=0.0,
+         weight_decay_mask=None, mu_dtype=None, *, nesterov: bool = True, adaptive: bool = False,
+         preconditioning: str = "frobenius", adam_b1=0.9, adam_b2=0.999, adam_eps=None, adam_eps_root=0.0,
+         adam_weight_decay=None, adam_learning_rate=None, muon_weight_dimension_numbers=None,
+         consistent_rms=None, orthogonalize_fn=orthogonalize_via_newton_schulz,
+         momentum_accumulator: str = "ema", use_magma: bool = False, magma_p: float = 0.5,
+         magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
+    """muon.py:398-486: Muon with automatic Muon/AdamW partitioning."""
+    if adam_learning_rate is None:
+        adam_learning_rate = learning_rate
+    if adam_eps is None:
+        adam_eps = eps
+    eff_adam_wd = weight_decay if adam_weight_decay is None else adam_weight_decay
+    part = _make_matrix_partition_fns(muon_weight_dimension_numbers, "muon")
+    branch = _build_unscaled_muon_branch(
+        ns_coeffs=ns_coeffs, ns_steps=ns_steps, beta=beta, eps=eps, mu_dtype=mu_dtype, nesterov=nesterov,
+        adaptive=adaptive, preconditioning=preconditioning, weight_dimension_numbers=part.masked_specs,
+        orthogonalize_fn=orthogonalize_fn, momentum_accumulator=momentum_accumulator, use_magma=use_magma,
+        magma_p=magma_p, magma_tau=magma_tau, consistent_rms=consistent_rms, weight_decay=weight_decay,
+        weight_decay_mask=weight_decay_mask, axis_name=axis_name, key=key)
+    adam_tx = adamw(learning_rate=adam_learning_rate, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
+                    weight_decay=eff_adam_wd, weight_decay_mask=weight_decay_mask, mu_dtype=mu_dtype,
+                    nesterov=nesterov, use_magma=use_magma, magma_p=magma_p, magma_tau=magma_tau,
+                    axis_name=axis_name, key=key)
+    composite = partition({"muon": chain(branch, scale_by_learning_rate(learning_rate)), "adam": adam_tx},
+                          part.labels)
+    if orthogonalize_fn is not orthogonalize_via_newton_schulz:
+        return composite  # custom hook: run the chain transform by transform
+
+    muon_wd_on = has_nonzero_or_scheduled(weight_decay)
+    adam_wd_on = has_nonzero_or_scheduled(eff_adam_wd)
+
+    def fused_update(updates, state, params=None):
+        from . import distributed  # late import: optional torch.distributed plumbing
+
+        if params is None:
+            # scale_by_muon resolves the callable partition specs from params
+            # (dimension_numbers.py:127-132).
+            raise ValueError(
+                "`params` must be provided to `scale_by_muon` when `weight_dimension_numbers` is callable."
+            )
+        labels = part.labels(updates)
+        specs_tree = part.masked_specs(params)
+        leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
+        lab = tree_flatten(labels, is_leaf=lambda x: x is None or isinstance(x, str))[0]
+        specs = _flatten_specs(specs_tree, len(leaves))
+        ps = tree_flatten(params, is_leaf=is_aux_leaf)[0]
+        mask_tree = resolve_mask(weight_decay_mask, params)
+        masks = tree_flatten(mask_tree, is_leaf=is_aux_leaf)[0] if mask_tree is not None else [True] * len(leaves)
+
+        mstate = state.inner_states["muon"].inner_state  # ((MuonState, Empty, [wd]), lr_state)
+        astate = state.inner_states["adam"].inner_state  # (ScaleByAdamState, [wd], lr_state)
+        muon_st: MuonState = mstate[0][0]
+        mlr_state = mstate[1]
+        adam_st: ScaleByAdamState = astate[0]
+        alr_state = astate[-1]
+        lr = resolve_scalar(learning_rate, host_count(mlr_state.count)) if callable(learning_rate) else float(
+            learning_rate)
+        alr = resolve_scalar(adam_learning_rate, host_count(alr_state.count)) if callable(
+            adam_learning_rate) else float(adam_learning_rate)
+
+        mus = tree_flatten(muon_st.mu, is_leaf=is_aux_leaf)[0]
+        muon_leaves = [g if (not is_aux_leaf(g) and l == "muon") else None for g, l in zip(leaves, lab)]
+        muon_specs = [s if l == "muon" else None for s, l in zip(specs, lab)]
+        for g, s in zip(muon_leaves, muon_specs):
+            if g is not None:
+                _validate_matrix_operand(g, s, "scale_by_muon")
+        ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon")
+        scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
+        decays = []
+        for L in ml:
+            on = muon_wd_on and bool(masks[L.pos]) and L.p is not None
+            decays.append(round_to_dtype(float(weight_decay), L.p.dtype) if on else 0.0)
+        prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
+                                 accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
+                                 ns_steps=ns_steps, lr=lr, fuse_tail=1)
+        ctx = distributed.current()
+        if ctx is not None and ctx.world_size > 1:
+            outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr)
+        else:
+            _run_muon_update(ml, prm, cbuf, scales, decays)
+            outs = _finish_leaves(ml)
+
+        # AdamW fallback leaves.
+        a_items, a_pos = [], []
+        amus = tree_flatten(adam_st.mu, is_leaf=is_aux_leaf)[0]
+        anus = tree_flatten(adam_st.nu, is_leaf=is_aux_leaf)[0]
+        for i, (g, l) in enumerate(zip(leaves, lab)):
+            if is_aux_leaf(g) or l != "adam":
+                continue
+            require_cuda(g, "gradient")
+            if g.dtype.is_complex:
+                raise NotImplementedError("complex leaves are not on the B200 hot path")
+            p = ps[i]
+            on = adam_wd_on and bool(masks[i]) and p is not None and not is_aux_leaf(p)
+            out = torch.empty(g.shape, dtype=torch.float32, device=g.device)
+            if on:
+                a_items.append((g.contiguous(), amus[i], anus[i], p.contiguous(), out,
+                                round_to_dtype(float(eff_adam_wd), p.dtype), rf_dtype(p)))
+            else:
+                a_items.append((g.contiguous(), amus[i], anus[i], None, out, 0.0, _lib.RF_F32))
+            a_pos.append(i)
+        run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
+                 count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
+
+        full = list(leaves)
+        for L, o in zip(ml, outs):
+            full[L.pos] = o
+        for i, it in zip(a_pos, a_items):
+            full[i] = it[4]
+
+        new_muon = MuonState(safe_increment(muon_st.count), muon_st.mu, muon_st.ns_coeffs, muon_st.magma_s,
+                             muon_st.key)
+        new_mlr = ScaleByScheduleState(safe_increment(mlr_state.count)) if callable(learning_rate) else mlr_state
+        new_adam = ScaleByAdamState(safe_increment(adam_st.count), adam_st.mu, adam_st.nu, adam_st.magma_s,
+                                    adam_st.key)
+        new_alr = ScaleByScheduleState(safe_increment(alr_state.count)) if callable(
+            adam_learning_rate) else alr_state
+        new_state = PartitionState({
+            "muon": MaskedState(((new_muon, *mstate[0][1:]), new_mlr)),
+            "adam": MaskedState((new_adam, *astate[1:-1], new_alr)),
+        })
+        return tree_unflatten(treedef, full), new_state
+
+    return GradientTransformation(composite.init, fused_update)
+
+
+__all__ = [
+    "MuonDimensionNumbers",
+    "MuonState",
+    "muon",
+    "orthogonalize_via_newton_schulz",
+    "polar_express_coeffs",
+    "resolve_ns_coeffs",
+    "scale_by_muon",
+    "scale_by_muon_shape",
+    "scale_by_shape",
+]

@@ -1,0 +1,358 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle and
+the committed golden fixtures.
+
+Tolerances (relative Frobenius error of the orthogonalised / final update):
+  * 16-bit Newton-Schulz operands (f16 default): <= 1e-2, the bar for a
+    16-bit NS against the reference's float32 NS; f16 typically lands near 2e-3.
+  * float32 NS mode: <= 1e-5.
+  * AdamW fallback leaves: <= 1e-6.
+  * momentum state: bit-exact (same float32 operation order as the reference).
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = os.path.join(HERE, "golden")
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(autouse=True)
+def _precision():
+    import rollfast_b200 as rf
+
+    rf.set_ns_precision("f16")
+    yield
+    rf.set_ns_precision("f16")
+
+
+def dev():
+    return torch.device("cuda:0")
+
+
+def to_dev(x, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev()).to(dtype)
+
+
+def ns_gpu(x, coeffs, steps, precision="f16"):
+    import rollfast_b200 as rf
+
+    rf.set_ns_precision(precision)
+    out = rf.orthogonalize_via_newton_schulz(
+        to_dev(x), torch.from_numpy(np.asarray(coeffs, np.float32)), steps, "frobenius", 1e-8,
+        rf.MatrixDimensionNumbers(1, 2) if x.ndim == 3 else None)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# Newton-Schulz (orthogonalize_fn seam) against the golden fixtures.
+# ---------------------------------------------------------------------------
+GOLD_NS = np.load(os.path.join(GOLD, "ns_small.npz"))
+
+
+@pytest.mark.parametrize("case", ["wide", "tall", "batched"])
+@pytest.mark.parametrize("sched,steps", [("standard5", 5), ("polar5", 5), ("polar8", 8), ("dion5", 5)])
+@pytest.mark.parametrize("precision,tol", [("f16", 1e-2), ("f32", 1e-5)])
+def test_ns_matches_golden(case, sched, steps, precision, tol):
+    x = GOLD_NS[f"x_{case}"]
+    ref = GOLD_NS[f"o_{case}_{sched}"]
+    got = ns_gpu(x, GOLD_NS[f"coeffs_{sched}"], steps, precision)
+    assert got.shape == ref.shape
+    assert np.all(np.isfinite(got))
+    assert rel(got, ref) <= tol, (case, sched, precision, rel(got, ref))
+
+
+@pytest.mark.parametrize("shape", [(4, 4), (17, 33), (33, 17), (256, 1024), (300, 700), (1024, 4096)])
+def test_ns_random_shapes_f16_and_f32(shape):
+    rng = np.random.default_rng(sum(shape))
+    x = rng.standard_normal(shape).astype(np.float32)
+    c = O.resolve_ns_coeffs("standard", 5)
+    ref = O.quintic_newton_schulz(x, c, 5)
+    got16 = ns_gpu(x, c, 5, "f16")
+    assert rel(got16, ref) <= 1e-2, rel(got16, ref)
+    got32 = ns_gpu(x, c, 5, "f32")
+    assert rel(got32, ref) <= 1e-5, rel(got32, ref)
+
+
+def test_ns_bf16_operands_close():
+    # bf16 operands carry 8 significand bits; their error sits near the 1e-2
+    # bar (the reason f16 operands are the default).
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((512, 2048)).astype(np.float32)
+    c = O.resolve_ns_coeffs("standard", 5)
+    ref = O.quintic_newton_schulz(x, c, 5)
+    got = ns_gpu(x, c, 5, "bf16")
+    assert rel(got, ref) <= 2.5e-2, rel(got, ref)
+
+
+def test_ns_f16_tighter_than_bar_on_full_rank_input():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((768, 2304)).astype(np.float32)
+    c = O.resolve_ns_coeffs("polar_express", 5)
+    ref = O.quintic_newton_schulz(x, c, 5)
+    got = ns_gpu(x, c, 5, "f16")
+    assert rel(got, ref) <= 5e-3, rel(got, ref)
+
+
+# ---------------------------------------------------------------------------
+# Full muon() steps against the golden fixtures (bf16 params, fp32 state).
+# ---------------------------------------------------------------------------
+GOLD_MU = np.load(os.path.join(GOLD, "muon_steps.npz"))
+
+
+def _golden_grads(shapes, step):
+    g = {k: O.bf16_round(np.random.default_rng(100 + step).standard_normal(s).astype(np.float32))
+         for k, s in shapes.items()}
+    g["b"] = np.random.default_rng(200 + step).standard_normal(shapes["b"]).astype(np.float32)
+    return g
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("ema_nesterov", dict()),
+    ("heavy_ball", dict(momentum_accumulator="heavy_ball", nesterov=False)),
+    ("polar", dict(ns_coeffs="polar_express")),
+])
+@pytest.mark.parametrize("precision,tol", [("f16", 1e-2), ("f32", 1e-5)])
+def test_muon_steps_match_golden(name, kw, precision, tol):
+    import rollfast_b200 as rf
+
+    rf.set_ns_precision(precision)
+    p_np = {k: GOLD_MU[f"p_{k}"] for k in ("w", "v", "b")}
+    params = {"w": to_dev(p_np["w"], torch.bfloat16), "v": to_dev(p_np["v"], torch.bfloat16),
+              "b": to_dev(p_np["b"], torch.float32)}
+    shapes = {k: v.shape for k, v in p_np.items()}
+    tx = rf.muon(learning_rate=0.02, weight_decay=0.01, **kw)
+    st = tx.init(params)
+    for step in range(3):
+        g = _golden_grads(shapes, step)
+        grads = {"w": to_dev(g["w"], torch.bfloat16), "v": to_dev(g["v"], torch.bfloat16),
+                 "b": to_dev(g["b"], torch.float32)}
+        u, st = tx.update(grads, st, params)
+        torch.cuda.synchronize()
+        for k in ("w", "v"):
+            assert u[k].dtype == torch.float32
+            e = rel(u[k].cpu().numpy(), GOLD_MU[f"{name}_u{step}_{k}"])
+            assert e <= tol, (name, step, k, e)
+        e = rel(u["b"].cpu().numpy(), GOLD_MU[f"{name}_u{step}_b"])
+        assert e <= 1e-6, ("adam", step, e)
+    mstate = st.inner_states["muon"].inner_state[0][0]
+    astate = st.inner_states["adam"].inner_state[0]
+    np.testing.assert_array_equal(mstate.mu["w"].cpu().numpy(), GOLD_MU[f"{name}_mu_w"])
+    np.testing.assert_array_equal(mstate.mu["v"].cpu().numpy(), GOLD_MU[f"{name}_mu_v"])
+    assert rel(astate.mu["b"].cpu().numpy(), GOLD_MU[f"{name}_adam_mu_b"]) <= 1e-6
+    assert rel(astate.nu["b"].cpu().numpy(), GOLD_MU[f"{name}_adam_nu_b"]) <= 1e-6
+    assert int(mstate.count) == 3 and int(astate.count) == 3
+
+
+# ---------------------------------------------------------------------------
+# one fp32 1024x4096 leaf + a 4096 fp32 bias, seed 0.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("precision,tol", [("f16", 1e-2), ("f32", 1e-5)])
+def test_config1_single_step(precision, tol):
+    import rollfast_b200 as rf
+
+    rf.set_ns_precision(precision)
+    rng = np.random.default_rng(0)
+    g_w = rng.standard_normal((1024, 4096)).astype(np.float32)
+    g_b = rng.standard_normal((4096,)).astype(np.float32)
+    p_w = np.zeros((1024, 4096), np.float32)
+    p_b = np.zeros((4096,), np.float32)
+    params_np = {"w": p_w, "b": p_b}
+    grads_np = {"w": g_w, "b": g_b}
+    ora = O.OracleMuon(learning_rate=0.02, beta=0.95, nesterov=True)
+    u_ref, st_ref = ora.update(grads_np, ora.init(params_np), params_np)
+    tx = rf.muon(learning_rate=0.02, beta=0.95, nesterov=True)
+    params = {k: to_dev(v) for k, v in params_np.items()}
+    u, st = tx.update({k: to_dev(v) for k, v in grads_np.items()}, tx.init(params), params)
+    torch.cuda.synchronize()
+    assert rel(u["w"].cpu().numpy(), u_ref["w"]) <= tol
+    assert rel(u["b"].cpu().numpy(), u_ref["b"]) <= 1e-6
+    mstate = st.inner_states["muon"].inner_state[0][0]
+    np.testing.assert_array_equal(mstate.mu["w"].cpu().numpy(), st_ref["mu"]["w"])
+
+
+# ---------------------------------------------------------------------------
+# BASELINE config 2 (GPT-2 small, stacked layers, polar_express), reduced to
+# 2 layers x 3 steps for the oracle; the full-size run is in the bench.
+# ---------------------------------------------------------------------------
+def test_config2_stacked_layers_reduced():
+    import rollfast_b200 as rf
+
+    L = 2
+    shapes = {"qkv": (L, 768, 2304), "proj": (L, 768, 768), "fc": (L, 768, 3072), "fc_out": (L, 3072, 768),
+              "ln_g": (L, 768), "emb": (5000, 768)}
+    specs = {k: (O.MatrixDimensionNumbers(1, 2) if len(s) == 3 else None) for k, s in shapes.items()}
+    specs_rf = {k: (rf.MatrixDimensionNumbers(1, 2) if len(s) == 3 else None) for k, s in shapes.items()}
+    rng = np.random.default_rng(5)
+    params_np = {k: O.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32)) for k, s in shapes.items()}
+    dts = {k: "bfloat16" for k in shapes}
+    kw = dict(learning_rate=0.02, weight_decay=0.01, ns_coeffs="polar_express", ns_steps=5)
+    ora = O.OracleMuon(muon_weight_dimension_numbers=specs, **kw)
+    tx = rf.muon(muon_weight_dimension_numbers=specs_rf, **kw)
+    ost = ora.init(params_np)
+    params = {k: to_dev(v, torch.bfloat16) for k, v in params_np.items()}
+    st = tx.init(params)
+    for step in range(3):
+        gr = np.random.default_rng(50 + step)
+        g_np = {k: O.bf16_round(gr.standard_normal(s).astype(np.float32)) for k, s in shapes.items()}
+        u_ref, ost = ora.update(g_np, ost, params_np, param_dtypes=dts)
+        u, st = tx.update({k: to_dev(v, torch.bfloat16) for k, v in g_np.items()}, st, params)
+        torch.cuda.synchronize()
+        for k in shapes:
+            e = rel(u[k].cpu().numpy(), u_ref[k])
+            tol = 1e-2 if specs[k] is not None else 1e-6
+            assert e <= tol, (step, k, e)
+
+
+# ---------------------------------------------------------------------------
+# Reference behaviour tests (tests/test_muon.py) on the GPU path.
+# ---------------------------------------------------------------------------
+def test_isotropic_direction_has_equal_singular_values():
+    import rollfast_b200 as rf
+
+    params = {"w": torch.eye(4, device=dev())}
+    tx = rf.scale_by_muon(beta=0.0, nesterov=False, ns_steps=5,
+                          weight_dimension_numbers={"w": rf.MuonDimensionNumbers()})
+    u, _ = tx.update({"w": torch.eye(4, device=dev())}, tx.init(params), params)
+    s = np.linalg.svd(u["w"].cpu().numpy(), compute_uv=False)
+    assert u["w"].shape == (4, 4) and np.all(np.isfinite(s))
+    np.testing.assert_allclose(s, s[0], rtol=1e-6, atol=1e-6)
+
+
+def test_partition_routes_vectors_to_adamw_and_updates_negative():
+    import rollfast_b200 as rf
+
+    params = {"w": (torch.arange(1, 17, dtype=torch.float32, device=dev()).reshape(4, 4) / 10.0),
+              "b": torch.ones(4, device=dev())}
+    grads = {k: torch.full_like(v, 0.1) for k, v in params.items()}
+    tx = rf.muon(learning_rate=0.01, ns_steps=2)
+    u, _ = tx.update(grads, tx.init(params), params)
+    assert u["w"].shape == (4, 4) and u["b"].shape == (4,)
+    assert torch.all(torch.isfinite(u["w"])) and torch.all(torch.isfinite(u["b"]))
+    assert torch.all(u["w"] < 0)
+
+
+def test_conv_kernel_dimension_numbers():
+    import rollfast_b200 as rf
+
+    params = {"kernel": torch.ones((8, 3, 3, 4), device=dev())}
+    grads = {"kernel": torch.full_like(params["kernel"], 0.01)}
+    specs = {"kernel": rf.MuonDimensionNumbers(reduction_axis=(1, 2, 3), output_axis=0)}
+    tx = rf.muon(learning_rate=0.01, ns_steps=2, muon_weight_dimension_numbers=specs)
+    u, _ = tx.update(grads, tx.init(params), params)
+    assert u["kernel"].shape == params["kernel"].shape
+    assert torch.all(torch.isfinite(u["kernel"]))
+    # Against the oracle on the same input.
+    ora = O.OracleMuon(learning_rate=0.01, ns_steps=2, muon_weight_dimension_numbers={
+        "kernel": O.MatrixDimensionNumbers((1, 2, 3), 0)})
+    pn = {"kernel": np.ones((8, 3, 3, 4), np.float32)}
+    ur, _ = ora.update({"kernel": np.full((8, 3, 3, 4), 0.01, np.float32)}, ora.init(pn), pn)
+    assert rel(u["kernel"].cpu().numpy(), ur["kernel"]) <= 1e-2
+
+
+def test_fallback_adam_inherits_weight_decay():
+    import rollfast_b200 as rf
+
+    params = {"w": torch.ones((4, 4), device=dev()), "b": torch.ones(4, device=dev())}
+    grads = {k: torch.zeros_like(v) for k, v in params.items()}
+    mask = {"w": False, "b": True}
+    a = rf.muon(learning_rate=1.0, ns_steps=2, beta=0.0, nesterov=False, weight_decay=0.2, weight_decay_mask=mask)
+    b = rf.muon(learning_rate=1.0, ns_steps=2, beta=0.0, nesterov=False, weight_decay=0.2, adam_weight_decay=0.0,
+                weight_decay_mask=mask)
+    ua, _ = a.update(grads, a.init(params), params)
+    ub, _ = b.update(grads, b.init(params), params)
+    torch.testing.assert_close(ua["b"], -0.2 * params["b"])
+    torch.testing.assert_close(ub["b"], torch.zeros_like(params["b"]))
+
+
+def test_custom_orthogonalize_hook_receives_ordered_schedule():
+    import rollfast_b200 as rf
+
+    captured = {}
+
+    def hook(x, ns_coeffs, ns_steps, preconditioning, eps, dimension_numbers):
+        captured["coeffs"] = ns_coeffs
+        captured["x"] = x.clone()
+        return torch.ones((2, 2), device=x.device)
+
+    params = {"w": torch.ones((2, 2), device=dev())}
+    grads = {"w": torch.ones((2, 2), device=dev())}
+    coeffs = ((1.0, 0.0, 0.0), (2.0, 0.0, 0.0), (3.0, 0.0, 0.0))
+    tx = rf.scale_by_muon(ns_coeffs=coeffs, ns_steps=2, orthogonalize_fn=hook)
+    u, _ = tx.update(grads, tx.init(params), params)
+    np.testing.assert_allclose(captured["coeffs"].numpy(), ((1.0, 0.0, 0.0), (2.0, 0.0, 0.0)))
+    # The hook saw the Nesterov / bias-corrected direction.
+    _, d = O.momentum_runtime(np.ones((2, 2), np.float32), np.zeros((2, 2), np.float32), 0, 0.95, nesterov=True)
+    np.testing.assert_allclose(captured["x"].cpu().numpy(), d, rtol=1e-6)
+    torch.testing.assert_close(u["w"], torch.ones((2, 2), device=dev()))
+
+
+def test_scale_by_adam_matches_oracle_three_steps():
+    import rollfast_b200 as rf
+
+    g = torch.tensor([0.1, -0.2], device=dev())
+    params = {"w": torch.tensor([1.0, -2.0], device=dev())}
+    tx = rf.scale_by_adam(b1=0.9, b2=0.999, eps=1e-8)
+    st = tx.init(params)
+    mu = nu = np.zeros(2, np.float32)
+    for c in range(3):
+        u, st = tx.update({"w": g}, st, params)
+        ur, mu, nu = O.adam_leaf_update(g.cpu().numpy(), mu, nu, c)
+        assert rel(u["w"].cpu().numpy(), ur) <= 1e-6
+
+
+def test_fp32_and_f16_paths_agree_on_llama_layer_shapes():
+    """Full Llama-3-8B layer shapes (4096x4096, 4096x1024, 4096x14336,
+    14336x4096): the tensor-core f16 path against the float32 CUDA-core path
+    (itself pinned to the oracle above), one step, same inputs."""
+    import rollfast_b200 as rf
+
+    torch.manual_seed(0)
+    shapes = {"q": (4096, 4096), "k": (4096, 1024), "gate": (4096, 14336), "down": (14336, 4096)}
+    params = {k: (torch.randn(s, device=dev()) * 0.02).to(torch.bfloat16) for k, s in shapes.items()}
+    grads = {k: torch.randn(s, device=dev()).to(torch.bfloat16) for k, s in shapes.items()}
+    outs = {}
+    for prec in ("f32", "f16"):
+        rf.set_ns_precision(prec)
+        tx = rf.muon(learning_rate=0.02, weight_decay=0.01)
+        u, _ = tx.update(grads, tx.init(params), params)
+        torch.cuda.synchronize()
+        outs[prec] = {k: v.cpu().numpy() for k, v in u.items()}
+    for k in shapes:
+        e = rel(outs["f16"][k], outs["f32"][k])
+        assert e <= 1e-2, (k, e)
+
+
+def test_invalid_inputs_raise_value_errors():
+    import rollfast_b200 as rf
+
+    with pytest.raises(ValueError):
+        rf.scale_by_muon(beta=1.0)
+    with pytest.raises(ValueError, match="Not enough coeffs"):
+        rf.orthogonalize_via_newton_schulz(torch.ones((4, 4), device=dev()),
+                                           torch.tensor([[1.0, 0.0, 0.0]]), 2)
+    with pytest.raises(ValueError):
+        rf.orthogonalize_via_newton_schulz(torch.ones((2, 3, 4), device=dev()),
+                                           torch.tensor([1.0, 0.0, 0.0]), 2)
+
+
+def test_library_loaded_from_tree_and_counts_launches():
+    from rollfast_b200 import _lib
+
+    before = _lib.kernel_launch_count()
+    ns_gpu(np.ones((8, 8), np.float32), O.resolve_ns_coeffs("standard", 5), 5)
+    assert _lib.kernel_launch_count() > before
+    _lib.sync_check(torch.cuda.current_stream().cuda_stream)
