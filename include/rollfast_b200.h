@@ -71,9 +71,12 @@ typedef struct rf_muon_params {
   int32_t count;         /* state.count before this step (0-based) */
   int32_t nesterov;      /* muon.py:408 */
   int32_t accumulator;   /* rf_accumulator */
-  int32_t ns_steps;
-  int32_t n_coeff_rows;  /* 1 for a (3,) array, else rows of an (n,3) schedule (>= ns_steps) */
-  const float* coeffs;   /* HOST pointer: n_coeff_rows * 3 floats (a,b,c) */
+  int32_t ns_steps;      /* iterations when coeffs is a single (a,b,c) triple */
+  /* 0: coeffs is one (a,b,c) triple applied ns_steps times (fori_loop,
+   * orthogonalization.py:253-260); n > 0: coeffs is an ordered (n,3)
+   * schedule and exactly n iterations run (lax.scan, orthogonalization.py:262-269). */
+  int32_t n_coeff_rows;
+  const float* coeffs;   /* HOST pointer: max(1, n_coeff_rows) * 3 floats (a,b,c) */
   int32_t precision;     /* rf_ns_precision */
   float lr;              /* learning rate at this step (scale_by_learning_rate) */
   int32_t fuse_tail;     /* 1: out = -lr*(scale*O + decay*p); 0: out = O (leaf layout) */
@@ -96,7 +99,8 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
 rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
                             void* stream);
 
-/* The orthogonalize_fn seam: out = NS(x) over [batch][rows][cols]. */
+/* The orthogonalize_fn seam: out = NS(x) over [batch][rows][cols]
+ * (coeffs / n_coeff_rows / ns_steps as in rf_muon_params). */
 rf_status rf_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols,
                                           int32_t precision, size_t* bytes);
 rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
@@ -132,7 +136,12 @@ typedef struct rf_adam_leaf {
   int32_t decay_rounding;
 } rf_adam_leaf;
 typedef struct rf_adam_params {
-  float b1, b2, eps, eps_root;
+  /* b1, b2 as the caller's double-precision scalars: the reference forms
+   * (1.0 - b2) and (1.0 - b1) from Python floats before the float32 cast
+   * (utils.py:486, adam.py:154), but 1 - float32(b1) for the first moment
+   * (utils.py:333). */
+  double b1, b2;
+  float eps, eps_root;
   int32_t count;      /* state.count before this step */
   int32_t nesterov;
   float lr;

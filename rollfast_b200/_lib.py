@@ -108,8 +108,8 @@ class RfAdamLeaf(ctypes.Structure):
 
 class RfAdamParams(ctypes.Structure):
     _fields_ = [
-        ("b1", ctypes.c_float),
-        ("b2", ctypes.c_float),
+        ("b1", ctypes.c_double),
+        ("b2", ctypes.c_double),
         ("eps", ctypes.c_float),
         ("eps_root", ctypes.c_float),
         ("count", ctypes.c_int32),

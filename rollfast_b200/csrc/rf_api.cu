@@ -288,7 +288,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       uint8_t* xc = X0;
       uint8_t* xn = X1;
       for (int it = 0; it < ns_steps; ++it) {
-        const float* cf = coeffs + 3 * (n_coeff_rows == 1 ? 0 : it);
+        const float* cf = coeffs + 3 * (n_coeff_rows == 0 ? 0 : it);
         const float ca = cf[0], cb = cf[1], cc = cf[2];
         // A~ = (sa / sx^2) X~ X~^T
         ga.stage = kSyrkXXt;
@@ -349,11 +349,13 @@ static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vec
   return RF_OK;
 }
 
-static rf_status check_coeffs(const float* coeffs, int n_rows, int steps) {
-  if (steps < 1) return fail(RF_EINVAL, "ns_steps must be >= 1");
+// Number of NS iterations: a triple repeats ns_steps times, a schedule runs
+// all of its rows.
+static rf_status check_coeffs(const float* coeffs, int n_rows, int steps, int* iters) {
   if (!coeffs) return fail(RF_EINVAL, "coeffs must be non-null");
-  if (n_rows < 1) return fail(RF_EINVAL, "n_coeff_rows must be >= 1");
-  if (n_rows > 1 && n_rows < steps) return fail(RF_EINVAL, "Not enough coeffs to perform ns_steps steps");
+  if (n_rows < 0) return fail(RF_EINVAL, "n_coeff_rows must be >= 0");
+  if (n_rows == 0 && steps < 1) return fail(RF_EINVAL, "ns_steps must be >= 1");
+  *iters = n_rows == 0 ? steps : n_rows;
   return RF_OK;
 }
 
@@ -400,12 +402,13 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   if (p.accumulator != RF_EMA && p.accumulator != RF_HEAVY_BALL)
     return fail(RF_EINVAL, "momentum_accumulator must be 'ema' or 'heavy_ball'");
   if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
-  RF_TRY(check_coeffs(p.coeffs, p.n_coeff_rows, p.ns_steps));
+  int iters = 0;
+  RF_TRY(check_coeffs(p.coeffs, p.n_coeff_rows, p.ns_steps, &iters));
   std::vector<LeafPlan> lp;
   RF_TRY(leaves_from_abi(leaves, n_leaves, lp, true));
   Plan P;
   RF_TRY(build_plan(lp, p.precision, P));
-  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, p.ns_steps, p.eps, p.fuse_tail, p.lr,
+  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.fuse_tail, p.lr,
                       workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -484,12 +487,13 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
   if (!x || !out) return fail(RF_EINVAL, "x and out must be non-null");
   if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(RF_EINVAL, "bad dtype");
   if (!(eps > 0.f)) return fail(RF_EINVAL, "eps must be positive");
-  RF_TRY(check_coeffs(coeffs, n_coeff_rows, ns_steps));
+  int iters = 0;
+  RF_TRY(check_coeffs(coeffs, n_coeff_rows, ns_steps, &iters));
   Plan P;
   RF_TRY(ns_plan(batch, rows, cols, precision, P, x, x_dtype, out, out_dtype));
   MomentumCoeffs mc{};
   mc.mode = kDirIdentity;
-  return run_pipeline(P, mc, coeffs, n_coeff_rows, ns_steps, eps, 0, 0.f, workspace, workspace_bytes,
+  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, 0, 0.f, workspace, workspace_bytes,
                       static_cast<cudaStream_t>(stream));
 }
 
@@ -533,14 +537,15 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
   if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
   AdamCoeffs c{};
   const int t = p.count + 1;
-  c.b1 = p.b1;
-  c.b2 = p.b2;
-  c.one_minus_b1 = 1.0f - p.b1;                  // utils.py:333 (1 - decay32)
-  c.one_minus_b2 = float(1.0 - double(p.b2));     // utils.py:486 ((1.0 - decay) with a Python float)
-  c.one_minus_b1_py = float(1.0 - double(p.b1));  // adam.py:154 ((1.0 - b1) with a Python float)
-  c.bc1 = 1.0f - f32_pow(p.b1, t);                // adam.py:137
-  c.bc1_next = 1.0f - f32_pow(p.b1, t + 1);       // adam.py:141
-  c.bc2 = 1.0f - f32_pow(p.b2, t);                // adam.py:138
+  const float b1f = float(p.b1), b2f = float(p.b2);
+  c.b1 = b1f;
+  c.b2 = b2f;
+  c.one_minus_b1 = 1.0f - b1f;                 // utils.py:333 (1 - decay32)
+  c.one_minus_b2 = float(1.0 - p.b2);          // utils.py:486 ((1.0 - decay) with a Python float)
+  c.one_minus_b1_py = float(1.0 - p.b1);       // adam.py:154 ((1.0 - b1) with a Python float)
+  c.bc1 = 1.0f - f32_pow(b1f, t);              // adam.py:137
+  c.bc1_next = 1.0f - f32_pow(b1f, t + 1);     // adam.py:141
+  c.bc2 = 1.0f - f32_pow(b2f, t);              // adam.py:138
   c.eps = p.eps;
   c.eps_root = p.eps_root;
   c.neg_lr = -p.lr;

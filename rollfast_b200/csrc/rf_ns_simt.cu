@@ -23,7 +23,8 @@ __global__ void __launch_bounds__(ST) k_ns_simt(const __grid_constant__ NsGemmAr
   const int64_t K = stage == kSyrkXXt ? a.np : a.mp;
   const int64_t ldc = sym ? a.mp : a.np;
   const T* A = static_cast<const T*>(a.a_op) + gm * a.mp * K;
-  const T* B = static_cast<const T*>(a.b_op) + gm * a.mp * K;  // sym: same shape as A; BX: [mp][np]
+  // sym: B has A's shape [mp][K]; BX: B is X~ [mp][np].
+  const T* B = static_cast<const T*>(a.b_op) + gm * a.mp * (sym ? K : a.np);
   __shared__ float As[SK][SB + 4];
   __shared__ float Bs[SK][SB + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;

@@ -176,7 +176,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     key = tuple((L.layout.flat_shape, L.g.dtype) for L in ml)
     plan = ctx.plans.get(key)
     if plan is None:
-        steps = prm.ns_steps
+        steps = prm.n_coeff_rows or prm.ns_steps
         costs = [ns_flops(*L.layout.flat_shape) * steps for L in ml]
         plan = make_plan(sizes, costs, ctx.world_size, ctx.buckets)
         ctx.plans[key] = plan

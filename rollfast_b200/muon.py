@@ -182,8 +182,6 @@ def _leaf_table(ml: list, scales, decays):
 
 def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail):
     cbuf, rows = coeff_buffer(ns_coeffs)
-    if rows > 1 and rows < int(ns_steps):
-        raise ValueError(f"Not enough coeffs to perform {ns_steps} steps")
     prm = _lib.RfMuonParams()
     prm.beta = float(beta)
     prm.eps = float(eps)

@@ -112,15 +112,17 @@ def resolve_ns_coeffs(ns_coeffs: NsCoeffs, ns_steps) -> torch.Tensor:
 _resolve_ns_coeffs = resolve_ns_coeffs
 
 
-def coeff_buffer(ns_coeffs: torch.Tensor):
-    """(ctypes float array, rows) for the C ABI."""
-    c = ns_coeffs.detach().to("cpu", torch.float32).contiguous()
-    if c.ndim not in (1, 2) or c.shape[-1] != 3:
+def coeff_buffer(ns_coeffs):
+    """(ctypes float array, n_coeff_rows) for the C ABI: rows 0 marks a single
+    (3,) triple repeated ns_steps times (orthogonalization.py:253-260); an
+    (n, 3) schedule runs all n rows in order (orthogonalization.py:262-269)."""
+    c = torch.as_tensor(ns_coeffs).detach().to("cpu", torch.float32).contiguous()
+    if c.ndim not in (1, 2) or c.shape[-1] != 3 or (c.ndim == 2 and c.shape[0] == 0):
         raise ValueError(
             f"Newton-Schulz coefficients must have shape (3,) or (n, 3), got {tuple(c.shape)}."
         )
     flat = c.reshape(-1).tolist()
-    return (ctypes.c_float * len(flat))(*flat), (1 if c.ndim == 1 else c.shape[0])
+    return (ctypes.c_float * len(flat))(*flat), (0 if c.ndim == 1 else c.shape[0])
 
 
 def quintic_newton_schulz(x: torch.Tensor, ns_coeffs: torch.Tensor, ns_steps: int = 5,
@@ -138,8 +140,6 @@ def quintic_newton_schulz(x: torch.Tensor, ns_coeffs: torch.Tensor, ns_steps: in
         raise ValueError(f"Input must have rank >= 2, got shape={tuple(x.shape)}.")
     require_cuda(x, "x")
     cbuf, rows = coeff_buffer(ns_coeffs)
-    if rows > 1 and rows < int(ns_steps):
-        raise ValueError(f"Not enough coeffs to perform {ns_steps} steps")
     xc = x.contiguous()
     if xc.dtype not in (torch.float32, torch.bfloat16, torch.float16):
         xc = xc.float()

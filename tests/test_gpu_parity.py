@@ -341,9 +341,8 @@ def test_invalid_inputs_raise_value_errors():
 
     with pytest.raises(ValueError):
         rf.scale_by_muon(beta=1.0)
-    with pytest.raises(ValueError, match="Not enough coeffs"):
-        rf.orthogonalize_via_newton_schulz(torch.ones((4, 4), device=dev()),
-                                           torch.tensor([[1.0, 0.0, 0.0]]), 2)
+    with pytest.raises(ValueError, match="shape"):
+        rf.orthogonalize_via_newton_schulz(torch.ones((4, 4), device=dev()), torch.tensor([1.0, 0.0]), 2)
     with pytest.raises(ValueError):
         rf.orthogonalize_via_newton_schulz(torch.ones((2, 3, 4), device=dev()),
                                            torch.tensor([1.0, 0.0, 0.0]), 2)
@@ -356,3 +355,19 @@ def test_library_loaded_from_tree_and_counts_launches():
     ns_gpu(np.ones((8, 8), np.float32), O.resolve_ns_coeffs("standard", 5), 5)
     assert _lib.kernel_launch_count() > before
     _lib.sync_check(torch.cuda.current_stream().cuda_stream)
+
+
+def test_schedule_runs_all_rows_and_triple_repeats():
+    """An (n,3) schedule is scanned row by row regardless of ns_steps; a
+    (3,) triple repeats ns_steps times (orthogonalization.py:253-269)."""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((64, 192)).astype(np.float32)
+    one = np.asarray([[3.4445, -4.7750, 2.0315]], np.float32)
+    ref1 = O.quintic_newton_schulz(x, one, 5)          # one iteration
+    got1 = ns_gpu(x, one, 5, "f32")
+    assert rel(got1, ref1) <= 1e-5
+    tri = np.asarray([3.4445, -4.7750, 2.0315], np.float32)
+    ref3 = O.quintic_newton_schulz(x, tri, 3)
+    got3 = ns_gpu(x, tri, 3, "f32")
+    assert rel(got3, ref3) <= 1e-5
+    assert rel(got1, got3) > 1e-3

@@ -69,9 +69,11 @@ def test_muon_update_rejects_bad_params_before_any_launch():
     assert lib.rf_muon_update(None, 0, ctypes.byref(prm), None, 0, None) == _lib.RF_EINVAL
     c = (ctypes.c_float * 3)(3.4445, -4.775, 2.0315)
     prm.coeffs = ctypes.cast(c, ctypes.POINTER(ctypes.c_float))
-    prm.n_coeff_rows = 2
+    prm.n_coeff_rows, prm.ns_steps = 0, 0
     assert lib.rf_muon_update(None, 0, ctypes.byref(prm), None, 0, None) == _lib.RF_EINVAL
-    assert b"Not enough coeffs" in lib.rf_last_error()
+    assert b"ns_steps" in lib.rf_last_error()
+    prm.n_coeff_rows = -1
+    assert lib.rf_muon_update(None, 0, ctypes.byref(prm), None, 0, None) == _lib.RF_EINVAL
 
 
 # ---------------------------------------------------------------------------
