@@ -272,6 +272,8 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         l.norm_index = lp.scale_index;
         l.transposed = lp.transposed;
         l.gdt = lp.gdt;
+        l.vec_ok = (lp.cols % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.g) % 16 == 0) &&
+                   (!lp.mu || reinterpret_cast<uintptr_t>(lp.mu) % 16 == 0);
         FinalLeaf& f = ga.final_leaf[ga.n_final++];
         f.out = lp.out;
         f.p = lp.p;
@@ -281,9 +283,15 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         f.p_dtype = lp.pdt;
         f.shape_scale = lp.shape_scale;
         f.decay = lp.decay;
+        f.vec_ok = (gp.n % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
+                   (!lp.p || reinterpret_cast<uintptr_t>(lp.p) % 16 == 0);
         gm += lp.batch;
       }
-      RF_TRY(launch_ns_load(ld, P.precision, st));
+      for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
+        bool any = false;
+        for (int li : sub) any |= P.leaves[li].gdt == gdt;
+        if (any) RF_TRY(launch_ns_load(ld, gdt, P.precision, st));
+      }
 
       uint8_t* xc = X0;
       uint8_t* xn = X1;

@@ -185,53 +185,125 @@ __global__ void __launch_bounds__(kEwThreads) k_norm_finalize(const __grid_const
 
 // ---------------------------------------------------------------------------
 // k_ns_load: builds the padded NS operand X~0 = round(sx * (d / (||d|| + eps)))
-// for every matrix of one shape group.  64x64 output tiles; a transposed leaf
-// (rows > cols) is read along its rows and written along the NS rows through
-// shared memory, so both sides stay coalesced.
+// for every matrix of one shape group, 64x64 output tiles.  Each thread
+// moves 8-element vectors (16-byte grad / operand accesses, 32-byte mu).
+// A leaf with rows <= cols maps straight onto the operand; a transposed leaf
+// (rows > cols) is staged through shared memory so that both the leaf rows
+// and the operand rows are read and written contiguously.
 // ---------------------------------------------------------------------------
+template <int GDT>
+__device__ __forceinline__ void load8_any(const void* p, int64_t i, float* v) {
+  GradVec<GDT>::load8(p, i, v);
+}
+
 template <typename OT>
+__device__ __forceinline__ void store8(OT* p, const float* v);
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float* v) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float* v) {
+  uint4 u;
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// 8 consecutive scaled directions of leaf row `ir`, columns ic..ic+7 (zero
+// outside the leaf).
+template <int GDT>
+__device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int64_t base, int64_t ir, int64_t ic,
+                                     float denom, float* v) {
+  if (ir < L.rows && ic + 7 < L.cols && L.vec_ok) {
+    const int64_t idx = base + ir * L.cols + ic;
+    float g[8], m[8];
+    load8_any<GDT>(L.g, idx, g);
+    if (L.mu) {
+      const float4* mp = reinterpret_cast<const float4*>(L.mu + idx);
+      const float4 a = mp[0], b = mp[1];
+      m[0] = a.x; m[1] = a.y; m[2] = a.z; m[3] = a.w; m[4] = b.x; m[5] = b.y; m[6] = b.z; m[7] = b.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fdiv_rn(direction(P.c, g[k], m[k]), denom), P.sx);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int64_t c = ic + k;
+      float x = 0.f;
+      if (ir < L.rows && c < L.cols) {
+        const int64_t idx = base + ir * L.cols + c;
+        const float g = ld_as_float(L.g, GDT, idx);
+        const float m = L.mu ? L.mu[idx] : 0.f;
+        x = __fmul_rn(__fdiv_rn(direction(P.c, g, m), denom), P.sx);
+      }
+      v[k] = x;
+    }
+  }
+}
+
+template <int GDT, typename OT>
 __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLaunch P) {
   __shared__ float tile[64][65];
   __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
   for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].group_mat_begin;
   __syncthreads();
-  const int64_t tiles_r = P.mp / 64, tiles_c = P.np / 64;
-  const int64_t tiles_per_mat = tiles_r * tiles_c;
+  const int64_t tiles_c = P.np / 64;
+  const int64_t tiles_per_mat = (P.mp / 64) * tiles_c;
   const int64_t total = tiles_per_mat * P.group_mats;
+  const int tr = threadIdx.x >> 3;        // 0..31: tile row (and +32)
+  const int tc = (threadIdx.x & 7) * 8;   // 0..56: 8-column group
   for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
     const int64_t gm = t / tiles_per_mat;
     const int64_t tl = t - gm * tiles_per_mat;
     const int64_t r0 = (tl / tiles_c) * 64, c0 = (tl % tiles_c) * 64;
-    const int li = find_leaf(s_begin, P.n, gm);
-    const LoadLeaf& L = P.leaf[li];
+    const LoadLeaf& L = P.leaf[find_leaf(s_begin, P.n, gm)];
+    if (L.gdt != GDT) continue;  // uniform per tile: another launch covers it
     const int64_t bi = gm - L.group_mat_begin;
-    const int64_t numel = L.rows * L.cols;
-    const int64_t base = bi * numel;
+    const int64_t base = bi * L.rows * L.cols;
     const float denom = P.denom[L.norm_index + bi];
-    // Input tile: rows ir0.., cols ic0.. of the leaf matrix (rows x cols).
-    const int64_t ir0 = L.transposed ? c0 : r0;
-    const int64_t ic0 = L.transposed ? r0 : c0;
-    __syncthreads();
-    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
-      const int ii = e >> 6, jj = e & 63;
-      const int64_t ir = ir0 + ii, ic = ic0 + jj;
-      float v = 0.f;
-      if (ir < L.rows && ic < L.cols) {
-        const int64_t idx = base + ir * L.cols + ic;
-        const float g = ld_as_float(L.g, L.gdt, idx);
-        const float m = L.mu ? L.mu[idx] : 0.f;
-        // X / (||X|| + eps) as the reference divides, then the exact
-        // power-of-two operand scale.
-        v = __fmul_rn(__fdiv_rn(direction(P.c, g, m), denom), P.sx);
-      }
-      tile[ii][jj] = v;
-    }
-    __syncthreads();
     OT* out = static_cast<OT*>(P.x) + gm * P.mp * P.np;
-    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
-      const int ii = e >> 6, jj = e & 63;  // output (r0+ii, c0+jj)
-      const float v = L.transposed ? tile[jj][ii] : tile[ii][jj];
-      out[(r0 + ii) * P.np + (c0 + jj)] = from_float<OT>(v);
+    if (!L.transposed) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int64_t r = r0 + tr + 32 * h;
+        float v[8];
+        dir8<GDT>(P, L, base, r, c0 + tc, denom, v);
+        store8<OT>(out + r * P.np + c0 + tc, v);
+      }
+    } else {
+      // Operand (r, c) = leaf (c, r): read leaf rows c0.., columns r0..
+      __syncthreads();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int lr = tr + 32 * h;
+        float v[8];
+        dir8<GDT>(P, L, base, c0 + lr, r0 + tc, denom, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) tile[lr][tc + k] = v[k];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int orow = tr + 32 * h;
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = tile[tc + k][orow];
+        store8<OT>(out + (r0 + orow) * P.np + c0 + tc, v);
+      }
     }
   }
 }
@@ -334,13 +406,20 @@ rf_status launch_norm_finalize(const MomentumLaunch& P, float* denom, float eps,
   return check_launch("k_norm_finalize");
 }
 
-rf_status launch_ns_load(const LoadLaunch& P, int precision, cudaStream_t st) {
+template <int GDT>
+static void launch_load_g(const LoadLaunch& P, int precision, int grid, cudaStream_t st) {
+  if (precision == RF_NS_F16) k_ns_load<GDT, __half><<<grid, 256, 0, st>>>(P);
+  else if (precision == RF_NS_BF16) k_ns_load<GDT, __nv_bfloat16><<<grid, 256, 0, st>>>(P);
+  else k_ns_load<GDT, float><<<grid, 256, 0, st>>>(P);
+}
+
+rf_status launch_ns_load(const LoadLaunch& P, int gdt, int precision, cudaStream_t st) {
   const int64_t total = (P.mp / 64) * (P.np / 64) * P.group_mats;
   if (total == 0) return RF_OK;
   const int grid = int(total < int64_t(num_sms()) * 16 ? total : int64_t(num_sms()) * 16);
-  if (precision == RF_NS_F16) k_ns_load<__half><<<grid, 256, 0, st>>>(P);
-  else if (precision == RF_NS_BF16) k_ns_load<__nv_bfloat16><<<grid, 256, 0, st>>>(P);
-  else k_ns_load<float><<<grid, 256, 0, st>>>(P);
+  if (gdt == RF_F32) launch_load_g<RF_F32>(P, precision, grid, st);
+  else if (gdt == RF_BF16) launch_load_g<RF_BF16>(P, precision, grid, st);
+  else launch_load_g<RF_F16>(P, precision, grid, st);
   return check_launch("k_ns_load");
 }
 

@@ -55,7 +55,8 @@ struct LoadLeaf {
   int64_t group_mat_begin;   // first matrix of this leaf within the group
   int64_t norm_index;        // index of its first matrix in the denominator array
   int32_t transposed;
-  int32_t gdt;
+  int32_t gdt;               // grad dtype; a launch handles the leaves of one dtype
+  int32_t vec_ok;            // cols % 8 == 0 and 16-byte aligned grad / mu
 };
 
 struct LoadLaunch {
@@ -137,6 +138,7 @@ struct FinalLeaf {
   int64_t group_mat_begin;
   int32_t transposed;
   int32_t out_dtype, p_dtype;
+  int32_t vec_ok;  // out / p 16-byte aligned and n % 8 == 0: 32-column vector epilogue
   float shape_scale, decay;
 };
 
@@ -161,7 +163,7 @@ struct NsGemmArgs {
 
 rf_status launch_momentum_sumsq(const MomentumLaunch& P, int gdt, cudaStream_t st);
 rf_status launch_norm_finalize(const MomentumLaunch& P, float* denom, float eps, cudaStream_t st);
-rf_status launch_ns_load(const LoadLaunch& P, int precision, cudaStream_t st);
+rf_status launch_ns_load(const LoadLaunch& P, int gdt, int precision, cudaStream_t st);
 rf_status launch_adamw(const AdamLaunch& P, cudaStream_t st);
 rf_status launch_tail(const TailLaunch& P, cudaStream_t st);
 rf_status launch_direction(const DirLaunch& P, cudaStream_t st);
@@ -211,6 +213,78 @@ __device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf
     v = __fmul_rn(a.neg_lr, v);
   }
   st_from_float(L.out, L.out_dtype, idx, v);
+}
+
+// Vector form of final_store for 32 consecutive columns col0.. of row r of a
+// non-transposed leaf (requires FinalLeaf::vec_ok and col0 + 32 <= n).
+__device__ __forceinline__ void final_store32(const NsGemmArgs& a, const FinalLeaf& L, int64_t bi, int64_t r,
+                                              int64_t col0, const float* o) {
+  const int64_t idx = bi * a.m * a.n + r * a.n + col0;
+  float v[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] = o[k];
+  if (a.fuse_tail) {
+    float pv[32];
+    if (L.decay != 0.f) {
+      if (L.p_dtype == RF_F32) {
+        const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(L.p) + idx);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 x = q[j];
+          pv[4 * j] = x.x; pv[4 * j + 1] = x.y; pv[4 * j + 2] = x.z; pv[4 * j + 3] = x.w;
+        }
+      } else {
+        const uint4* q = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(L.p) + idx);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 u = q[j];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint16_t lo = uint16_t(w[h] & 0xFFFFu), hi = uint16_t(w[h] >> 16);
+            if (L.p_dtype == RF_BF16) {
+              pv[8 * j + 2 * h] = __bfloat162float(__ushort_as_bfloat16(lo));
+              pv[8 * j + 2 * h + 1] = __bfloat162float(__ushort_as_bfloat16(hi));
+            } else {
+              pv[8 * j + 2 * h] = __half2float(__ushort_as_half(lo));
+              pv[8 * j + 2 * h + 1] = __half2float(__ushort_as_half(hi));
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      float u = __fmul_rn(v[k], L.shape_scale);
+      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.p_dtype, L.decay, pv[k]));
+      v[k] = __fmul_rn(a.neg_lr, u);
+    }
+  }
+  if (L.out_dtype == RF_F32) {
+    float4* q = reinterpret_cast<float4*>(static_cast<float*>(L.out) + idx);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint4* q = reinterpret_cast<uint4*>(static_cast<uint16_t*>(L.out) + idx);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float x0 = v[8 * j + 2 * h], x1 = v[8 * j + 2 * h + 1];
+        uint16_t lo, hi;
+        if (L.out_dtype == RF_BF16) {
+          lo = __bfloat16_as_ushort(__float2bfloat16_rn(x0));
+          hi = __bfloat16_as_ushort(__float2bfloat16_rn(x1));
+        } else {
+          lo = __half_as_ushort(__float2half_rn(x0));
+          hi = __half_as_ushort(__float2half_rn(x1));
+        }
+        w[h] = uint32_t(lo) | (uint32_t(hi) << 16);
+      }
+      q[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
 }
 
 }  // namespace rf

@@ -206,6 +206,14 @@ struct Vec16<__nv_bfloat16> {
   }
 };
 
+// 16-bit lane k (compile-time after unrolling) of 32 packed values.
+__device__ __forceinline__ uint16_t lane16(const uint4 (&p)[4], int k) {
+  const uint4& u = p[k >> 3];
+  const int w = (k >> 1) & 3;
+  const uint32_t word = w == 0 ? u.x : (w == 1 ? u.y : (w == 2 ? u.z : u.w));
+  return (k & 1) ? uint16_t(word >> 16) : uint16_t(word & 0xFFFFu);
+}
+
 __device__ __forceinline__ void record_error(int code, volatile int* abort_flag) {
   *abort_flag = 1;
   atomicCAS(&g_tc_error, 0, code);
@@ -396,7 +404,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint4 packed[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
-          const T* pv = reinterpret_cast<const T*>(packed);
+          uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
           if (col0 >= row) {
             uint4* op = reinterpret_cast<uint4*>(out + rbase);
 #pragma unroll
@@ -404,12 +412,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else {
 #pragma unroll
             for (int k = 0; k < 32; ++k)
-              if (col0 + k >= row) out[rbase + k] = pv[k];
+              if (col0 + k >= row) out16[rbase + k] = lane16(packed, k);
           }
 #pragma unroll
           for (int k = 0; k < 32; ++k) {
             const int64_t c = col0 + k;
-            if (c > row) out[mat_off + c * ldc + row] = pv[k];
+            if (c > row) out16[mat_off + c * ldc + row] = lane16(packed, k);
           }
         } else {
           const int64_t rbase = mat_off + row * ldc + col0;
@@ -426,10 +434,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           } else if (row < a.m) {
             const FinalLeaf& L = a.final_leaf[fl];
             const int64_t bi = g - L.group_mat_begin;
-#pragma unroll 4
-            for (int k = 0; k < 32; ++k) {
-              const int64_t c = col0 + k;
-              if (c < a.n) final_store(a, L, bi, row, c, f[k] * a.out_scale);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
+            if (!L.transposed && L.vec_ok && col0 + 32 <= a.n) {
+              final_store32(a, L, bi, row, col0, f);
+            } else {
+              // Transposed leaves: lanes hold consecutive rows, so each
+              // scalar store is coalesced across the warp.
+#pragma unroll
+              for (int k = 0; k < 32; ++k) {
+                const int64_t c = col0 + k;
+                if (c < a.n) final_store(a, L, bi, row, c, f[k]);
+              }
             }
           }
         }
