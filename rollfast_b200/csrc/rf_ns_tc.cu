@@ -17,6 +17,7 @@
 // an error code, drains its own in-flight copies/MMAs and frees TMEM.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -466,6 +467,373 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ===========================================================================
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): one 256x256 tile per
+// pair.  CTA rank r loads A rows [128r, 128r+128) and its half of B
+// (N columns [128r, 128r+128)) with ordinary (non-multicast) TMA loads that
+// complete on the leader's full barrier; the leader's single MMA thread
+// issues M=256 N=256 K=16 tcgen05.mma across both SMs' tensor cores, each
+// SM accumulating its 128 rows in its own TMEM.  Commits are multicast to
+// both CTAs' barriers; epilogue warps of both CTAs release the accumulator
+// on the leader's barrier.  Per-SM operand traffic is half that of the
+// single-CTA 128x256 tile for the same MMA rate.
+// ===========================================================================
+namespace tc2 {
+
+constexpr int BM = 128;                  // rows per CTA (256 per pair)
+constexpr int BNH = 128;                 // B rows/cols per CTA (256 per pair)
+constexpr int BK = 64, STAGES = 6;
+constexpr int A_BYTES = BM * BK * 2;     // 16 KB
+constexpr int B_BYTES = BNH * BK * 2;    // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+using tc::kTimeoutNs;
+using tc::smem_u32;
+using tc::globaltimer;
+using tc::mbar_init;
+using tc::mbar_try_wait;
+using tc::mbar_wait;
+using tc::mbar_arrive_expect_tx;
+using tc::tc_fence_before;
+using tc::tc_fence_after;
+using tc::sdesc;
+using tc::tmem_ld32;
+using tc::Vec16;
+using tc::lane16;
+using tc::record_error;
+
+struct Tc2Params {
+  NsGemmArgs a;
+  int64_t total_tiles;  // 256x256 tiles (sym: upper triangle only)
+  int tiles_i;          // 256-row blocks
+  int tiles_j;          // 256-col blocks
+  int num_kb;
+  int sym;
+  int b_mn_major;
+  uint32_t idesc;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+// Arrive on the barrier at this shared offset in both CTAs of the pair once
+// all prior tcgen05 operations of this thread complete.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void decode_tile2(const Tc2Params& P, int64_t t, int64_t& g, int& I, int& J) {
+  if (P.sym) {
+    const int q = P.tiles_j;  // square blocks; row block I holds q - I tiles (J >= I)
+    const int64_t per = int64_t(q) * (q + 1) / 2;
+    g = t / per;
+    int rem = int(t - g * per);
+    int i = 0;
+    while (rem >= q - i) {
+      rem -= q - i;
+      ++i;
+    }
+    I = i;
+    J = i + rem;
+  } else {
+    const int64_t per = int64_t(P.tiles_i) * P.tiles_j;
+    g = t / per;
+    const int rem = int(t - g * per);
+    J = rem / P.tiles_i;
+    I = rem - J * P.tiles_i;
+  }
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    k_ns_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const __grid_constant__ Tc2Params P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // [0,S) full (leader), [S,2S) empty, [2S,2S+2) acc full, [2S+2,2S+4) acc empty (leader)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(accf0 + 8 * s, 1);
+      mbar_init(acce0 + 8 * s, 8);  // 4 epilogue warps x 2 CTAs
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const NsGemmArgs& a = P.a;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t fills = 0;
+      bool ok = true;
+      for (int64_t t = pair; ok && t < P.total_tiles; t += npairs) {
+        int64_t g;
+        int I, J;
+        decode_tile2(P, t, g, I, J);
+        const int arow = I * 256 + int(rank) * BM;
+        const int bcol = J * 256 + int(rank) * BNH;
+        for (int kb = 0; kb < P.num_kb; ++kb) {
+          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag)) {
+            record_error(kDevTimeoutProducer, abort_flag);
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = full0 + 8 * stage;
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * STAGE_BYTES);
+          const uint32_t fb = map_to_rank(fb_local, 0);
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+          tma_load_3d_pair(sa, &tmA, fb, kb * BK, arow, int(g));
+          if (P.b_mn_major) {
+            tma_load_3d_pair(sb, &tmB, fb, bcol, kb * BK, int(g));
+            tma_load_3d_pair(sb + 8192, &tmB, fb, bcol + 64, kb * BK, int(g));
+          } else {
+            tma_load_3d_pair(sb, &tmB, fb, kb * BK, bcol, int(g));
+          }
+          ++fills;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: wait until the MMA released each of the last (up to STAGES)
+      // fills -- fill f is stage f % STAGES, and its release completes phase
+      // f / STAGES of that stage's empty barrier -- so no copy into this
+      // CTA's shared memory and no commit arrival on it is still pending.
+      for (int64_t f = fills > STAGES ? fills - STAGES : 0; f < fills; ++f) {
+        const uint32_t bar = empty0 + 8 * uint32_t(f % STAGES);
+        const uint32_t par = uint32_t((f / STAGES) & 1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(bar, par)) {
+          if (globaltimer() - t0 > kTimeoutNs) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      int tiles_done = 0;
+      for (int64_t t = pair; ok && t < P.total_tiles; t += npairs) {
+        if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort_flag)) {
+          record_error(kDevTimeoutMma, abort_flag);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * 256);
+        for (int kb = 0; kb < P.num_kb; ++kb) {
+          if (!mbar_wait(full0 + 8 * stage, phase, abort_flag)) {
+            record_error(kDevTimeoutMma, abort_flag);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
+            const uint64_t bd = P.b_mn_major ? sdesc(sb + k * 2048, 8192, 1024) : sdesc(sb + k * 32, 16, 1024);
+            mma_f16_pair(d_tmem, ad, bd, P.idesc, (kb | k) != 0);
+          }
+          mma_commit_pair(empty0 + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(accf0 + 8 * acc);
+        ++tiles_done;
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Drain: wait until both CTAs' epilogues released the last (up to two)
+      // tiles -- tile k used accumulator k % 2, and its release completes
+      // phase k / 2 of that accumulator's empty barrier -- so every MMA and
+      // every remote arrival has landed.
+      for (int k = tiles_done > 2 ? tiles_done - 2 : 0; k < tiles_done; ++k) {
+        const uint32_t bar = acce0 + 8 * uint32_t(k & 1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(bar, uint32_t((k >> 1) & 1))) {
+          if (globaltimer() - t0 > kTimeoutNs) break;
+        }
+      }
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5 of both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int row_local = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const T* aux = static_cast<const T*>(a.aux);
+    T* out = static_cast<T*>(a.out);
+    const bool sym = P.sym;
+    const int64_t ldc = sym ? a.mp : a.np;
+    for (int64_t t = pair; t < P.total_tiles; t += npairs) {
+      int64_t g;
+      int I, J;
+      decode_tile2(P, t, g, I, J);
+      if (!mbar_wait(accf0 + 8 * acc, acc_phase, abort_flag)) {
+        record_error(kDevTimeoutEpilogue, abort_flag);
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = int64_t(I) * 256 + int64_t(rank) * BM + row_local;
+      const int64_t mat_off = g * a.mp * ldc;
+      int fl = 0;
+      if (a.stage == kGemmBXFinal) fl = find_final_leaf(a, g);
+      for (int ch = 0; ch < 256 / 32; ++ch) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * 256 + ch * 32), v);
+        const int64_t col0 = int64_t(J) * 256 + ch * 32;
+        if (sym) {
+          if (col0 + 31 < row) continue;
+          const int64_t rbase = mat_off + row * ldc + col0;
+          float f[32];
+          if (a.stage == kSyrkPoly) {
+            const uint4* ap = reinterpret_cast<const uint4*>(aux + rbase);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) Vec16<T>::unpack(ap[q], f + 8 * q);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) f[k] = a.alpha * v[k];
+          }
+          uint4 packed[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
+          uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
+          if (col0 >= row) {
+            uint4* op = reinterpret_cast<uint4*>(out + rbase);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) op[q] = packed[q];
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (col0 + k >= row) out16[rbase + k] = lane16(packed, k);
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int64_t c = col0 + k;
+            if (c > row) out16[mat_off + c * ldc + row] = lane16(packed, k);
+          }
+        } else {
+          const int64_t rbase = mat_off + row * ldc + col0;
+          const uint4* xp = reinterpret_cast<const uint4*>(aux + rbase);
+          float f[32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xp[q], f + 8 * q);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
+          if (a.stage == kGemmBX) {
+            uint4* op = reinterpret_cast<uint4*>(out + rbase);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) op[q] = Vec16<T>::pack(f + 8 * q);
+          } else if (row < a.m) {
+            const FinalLeaf& L = a.final_leaf[fl];
+            const int64_t bi = g - L.group_mat_begin;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
+            if (!L.transposed && L.vec_ok && col0 + 32 <= a.n) {
+              final_store32(a, L, bi, row, col0, f);
+            } else {
+#pragma unroll
+              for (int k = 0; k < 32; ++k) {
+                const int64_t c = col0 + k;
+                if (c < a.n) final_store(a, L, bi, row, c, f[k]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(acce0 + 8 * acc, 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still touch its TMEM / shared memory
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+}  // namespace tc2
+
 // ---------------------------------------------------------------------------
 // Host side: tensor maps (driver entry point fetched through the runtime, so
 // the library does not link libcuda) and launch.
@@ -538,11 +906,72 @@ rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
 
 }  // namespace tc
 
+namespace tc {
+namespace tc2 {
+template <typename T>
+rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(k_ns_tc2<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return fail(RF_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err));
+  Tc2Params P;
+  P.a = a;
+  const bool sym = a.stage == kSyrkXXt || a.stage == kSyrkPoly;
+  P.sym = sym;
+  P.b_mn_major = sym ? 0 : 1;
+  P.tiles_i = int(a.mp / 256);
+  P.tiles_j = int((sym ? a.mp : a.np) / 256);
+  const int64_t K = a.stage == kSyrkXXt ? a.np : a.mp;
+  P.num_kb = int(K / BK);
+  P.total_tiles = sym ? a.G * int64_t(P.tiles_j) * (P.tiles_j + 1) / 2 : a.G * int64_t(P.tiles_i) * P.tiles_j;
+  const uint32_t fmt = a.precision == RF_NS_F16 ? 0u : 1u;
+  P.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(P.b_mn_major) << 16) | (uint32_t(256 >> 3) << 17) |
+            (uint32_t(256 >> 4) << 24);
+  CUtensorMap mA, mB;
+  RF_TRY(tc::make_map(&mA, a.a_op, a.precision, a.G, a.mp, K, BM));
+  if (sym) RF_TRY(tc::make_map(&mB, a.b_op, a.precision, a.G, a.mp, K, BNH));
+  else RF_TRY(tc::make_map(&mB, a.b_op, a.precision, a.G, a.mp, a.np, 64));
+  static int64_t pairs_max = [] {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(num_sms()), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_ns_tc2<T>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    return int64_t(n);
+  }();
+  const int64_t pairs = P.total_tiles < pairs_max ? P.total_tiles : pairs_max;
+  k_ns_tc2<T><<<unsigned(2 * pairs), NUM_THREADS, SMEM_BYTES, st>>>(mA, mB, P);
+  return check_launch("k_ns_tc2");
+}
+}  // namespace tc2
+}  // namespace tc
+
+// Tensor-core kernel choice: the CTA-pair kernel when it has a full wave of
+// 256x256 tiles, otherwise the single-CTA kernel (twice as many 128x256
+// tiles for small groups).  ROLLFAST_NS_KERNEL=1|2 forces one.
+static int tc_variant(const NsGemmArgs& a) {
+  const char* e = getenv("ROLLFAST_NS_KERNEL");
+  const int forced = e ? atoi(e) : 0;
+  if (forced == 1 || forced == 2) return forced;
+  const bool sym = a.stage == kSyrkXXt || a.stage == kSyrkPoly;
+  const int64_t q = a.mp / 256;
+  const int64_t tiles2 = sym ? a.G * q * (q + 1) / 2 : a.G * q * (a.np / 256);
+  return tiles2 >= num_sms() / 2 ? 2 : 1;
+}
+
 rf_status launch_ns_gemm_tc(const NsGemmArgs& a, cudaStream_t st) {
   if (a.mp % 256 || a.np % 256) return fail(RF_EINVAL, "tcgen05 NS path needs dims padded to 256");
   if (a.G > 0x7FFFFFFF) return fail(RF_EINVAL, "group too large");
-  if (a.precision == RF_NS_F16) return tc::launch_typed<__half>(a, st);
-  if (a.precision == RF_NS_BF16) return tc::launch_typed<__nv_bfloat16>(a, st);
+  const int v = tc_variant(a);
+  if (a.precision == RF_NS_F16) return v == 2 ? tc::tc2::launch_typed<__half>(a, st) : tc::launch_typed<__half>(a, st);
+  if (a.precision == RF_NS_BF16)
+    return v == 2 ? tc::tc2::launch_typed<__nv_bfloat16>(a, st) : tc::launch_typed<__nv_bfloat16>(a, st);
   return fail(RF_EINVAL, "tcgen05 path takes 16-bit operands");
 }
 

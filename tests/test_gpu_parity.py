@@ -371,3 +371,21 @@ def test_schedule_runs_all_rows_and_triple_repeats():
     got3 = ns_gpu(x, tri, 3, "f32")
     assert rel(got3, ref3) <= 1e-5
     assert rel(got1, got3) > 1e-3
+
+
+@pytest.mark.parametrize("variant", ["1", "2"])
+@pytest.mark.parametrize("shape,batch", [((256, 512), 1), ((512, 1024), 3), ((1024, 768), 2), ((768, 2304), 4)])
+def test_tensor_core_kernel_variants_match_oracle(variant, shape, batch, monkeypatch):
+    """Both tcgen05 kernels -- single-CTA 128x256 tiles and the CTA-pair
+    (cta_group::2) 256x256 tiles -- on symmetric and general stages,
+    batched, including transposed inputs (rows > cols)."""
+    monkeypatch.setenv("ROLLFAST_NS_KERNEL", variant)
+    rng = np.random.default_rng(batch * 7 + shape[0])
+    x = rng.standard_normal((batch,) + shape).astype(np.float32)
+    c = O.resolve_ns_coeffs("polar_express", 5)
+    ref = O.quintic_newton_schulz(x, c, 5)
+    got = ns_gpu(x if batch > 1 else x[0], c, 5, "f16")
+    got = got.reshape(ref.shape)
+    assert rel(got, ref) <= 1e-2, (variant, shape, batch, rel(got, ref))
+    from rollfast_b200 import _lib
+    _lib.sync_check(torch.cuda.current_stream().cuda_stream)
