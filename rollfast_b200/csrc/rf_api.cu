@@ -283,7 +283,9 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         f.p_dtype = lp.pdt;
         f.shape_scale = lp.shape_scale;
         f.decay = lp.decay;
-        f.vec_ok = (gp.n % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
+        // Runs of 32 along the leaf's rows: length n (NS columns) for a
+        // plain leaf, m (NS rows) for a transposed one.
+        f.vec_ok = ((lp.transposed ? gp.m : gp.n) % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
                    (!lp.p || reinterpret_cast<uintptr_t>(lp.p) % 16 == 0);
         gm += lp.batch;
       }

@@ -138,7 +138,7 @@ struct FinalLeaf {
   int64_t group_mat_begin;
   int32_t transposed;
   int32_t out_dtype, p_dtype;
-  int32_t vec_ok;  // out / p 16-byte aligned and n % 8 == 0: 32-column vector epilogue
+  int32_t vec_ok;  // out / p 16-byte aligned and the leaf's row length % 8 == 0: vector epilogue
   float shape_scale, decay;
 };
 
@@ -215,11 +215,12 @@ __device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf
   st_from_float(L.out, L.out_dtype, idx, v);
 }
 
-// Vector form of final_store for 32 consecutive columns col0.. of row r of a
-// non-transposed leaf (requires FinalLeaf::vec_ok and col0 + 32 <= n).
-__device__ __forceinline__ void final_store32(const NsGemmArgs& a, const FinalLeaf& L, int64_t bi, int64_t r,
-                                              int64_t col0, const float* o) {
-  const int64_t idx = bi * a.m * a.n + r * a.n + col0;
+// Vector form of final_store for 32 consecutive leaf elements starting at
+// linear index idx (a row run of a leaf, or a column run of a transposed
+// leaf).  Requires FinalLeaf::vec_ok (16-byte aligned pointers, run start a
+// multiple of 8).
+__device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const FinalLeaf& L, int64_t idx,
+                                                  const float* o) {
   float v[32];
 #pragma unroll
   for (int k = 0; k < 32; ++k) v[k] = o[k];
@@ -284,6 +285,44 @@ __device__ __forceinline__ void final_store32(const NsGemmArgs& a, const FinalLe
       }
       q[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
+  }
+}
+
+// Final-stage epilogue for one 32-column chunk held by a warp: lane l owns
+// row row0 + l (columns col0..col0+31, values o[], already scaled to O).  A
+// transposed leaf is stored along its rows, i.e. along the NS columns, so the
+// warp's 32x32 block is transposed through `stg` (32 x 33 floats, per warp)
+// and every lane writes one 32-element run.
+__device__ __forceinline__ void final_chunk(const NsGemmArgs& a, const FinalLeaf& L, int64_t bi, int64_t row0,
+                                           int64_t col0, int lane, const float* o, float* stg) {
+  const int64_t mat = bi * a.m * a.n;
+  if (!L.transposed) {
+    const int64_t r = row0 + lane;
+    if (r >= a.m) return;
+    if (L.vec_ok && col0 + 32 <= a.n) {
+      final_store_run32(a, L, mat + r * a.n + col0, o);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (col0 + k < a.n) final_store(a, L, bi, r, col0 + k, o[k]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k) stg[lane * 33 + k] = o[k];
+  __syncwarp();
+  float t[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) t[i] = stg[i * 33 + lane];
+  __syncwarp();
+  const int64_t c = col0 + lane;
+  if (c >= a.n) return;
+  if (L.vec_ok && row0 + 32 <= a.m) {
+    final_store_run32(a, L, mat + c * a.m + row0, t);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (row0 + i < a.m) final_store(a, L, bi, row0 + i, c, t[i]);
   }
 }
 

@@ -35,7 +35,8 @@ constexpr int B_BYTES = BN * BK * 2;             // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // per-warp 32x32 transpose buffers
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/ + EPI_STAGE_BYTES;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct TcParams {
@@ -220,6 +221,70 @@ __device__ __forceinline__ void record_error(int code, volatile int* abort_flag)
   atomicCAS(&g_tc_error, 0, code);
 }
 
+// One 32-column chunk of the epilogue.  The calling warp holds rows
+// row0..row0+31 (lane = row - row0) of matrix g, columns col0..col0+31 of the
+// accumulator in v[].  Stages: symmetric (upper-triangle store + mirror),
+// general (fused a X + B X), final (O, or the fused tail, into the leaf).
+template <typename T>
+__device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, int64_t g, int64_t row0, int64_t col0,
+                                               int lane, int fl, const float* v, float* stg) {
+  const T* aux = static_cast<const T*>(a.aux);
+  T* out = static_cast<T*>(a.out);
+  const int64_t ldc = sym ? a.mp : a.np;
+  const int64_t mat_off = g * a.mp * ldc;
+  const int64_t row = row0 + lane;
+  const int64_t rbase = mat_off + row * ldc + col0;
+  float f[32];
+  if (sym) {
+    if (col0 + 31 < row) return;  // whole chunk below the diagonal (no warp-collective work follows)
+    if (a.stage == kSyrkPoly) {
+      const uint4* ap = reinterpret_cast<const uint4*>(aux + rbase);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) Vec16<T>::unpack(ap[q], f + 8 * q);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) f[k] = a.alpha * v[k];
+    }
+    // Round once; the direct and mirrored copies hold the same value.
+    uint4 packed[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
+    uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
+    if (col0 >= row) {
+      uint4* op = reinterpret_cast<uint4*>(out + rbase);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) op[q] = packed[q];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (col0 + k >= row) out16[rbase + k] = lane16(packed, k);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int64_t c = col0 + k;
+      if (c > row) out16[mat_off + c * ldc + row] = lane16(packed, k);
+    }
+    return;
+  }
+  const uint4* xp = reinterpret_cast<const uint4*>(aux + rbase);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xp[q], f + 8 * q);
+#pragma unroll
+  for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
+  if (a.stage == kGemmBX) {
+    uint4* op = reinterpret_cast<uint4*>(out + rbase);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) op[q] = Vec16<T>::pack(f + 8 * q);
+    return;
+  }
+  const FinalLeaf& L = a.final_leaf[fl];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
+  final_chunk(a, L, g - L.group_mat_begin, row0, col0, lane, f, stg);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     k_ns_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -230,6 +295,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc full, [2S+2..2S+4) acc empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 4 x 32x33 floats
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -362,13 +428,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
-    const int row_local = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const T* aux = static_cast<const T*>(a.aux);
-    T* out = static_cast<T*>(a.out);
-    const bool sym = P.sym;
-    const int64_t ldc = sym ? a.mp : a.np;
+    float* stg = epi_stage + (warp - 2) * (32 * 33);
     for (int64_t t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
       int64_t g;
       int I, J;
@@ -378,78 +440,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = int64_t(I) * BM + row_local;
-      const int64_t mat_off = g * a.mp * ldc;
+      const int64_t row0 = int64_t(I) * BM + quarter * 32;
       int fl = 0;
       if (a.stage == kGemmBXFinal) fl = find_final_leaf(a, g);
       for (int ch = 0; ch < BN / 32; ++ch) {
         float v[32];
         __syncwarp();  // tcgen05.ld is warp-collective; lanes may have diverged on the diagonal
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + ch * 32), v);
-        const int64_t col0 = int64_t(J) * BN + ch * 32;
-        if (sym) {
-          if (col0 + 31 < row) continue;  // whole chunk below the diagonal
-          const int64_t rbase = mat_off + row * ldc + col0;
-          float f[32];
-          if (a.stage == kSyrkPoly) {
-            const uint4* ap = reinterpret_cast<const uint4*>(aux + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) Vec16<T>::unpack(ap[q], f + 8 * q);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] = a.alpha * v[k];
-          }
-          // Round once; the direct and mirrored copies hold the same value.
-          uint4 packed[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
-          uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
-          if (col0 >= row) {
-            uint4* op = reinterpret_cast<uint4*>(out + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) op[q] = packed[q];
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (col0 + k >= row) out16[rbase + k] = lane16(packed, k);
-          }
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int64_t c = col0 + k;
-            if (c > row) out16[mat_off + c * ldc + row] = lane16(packed, k);
-          }
-        } else {
-          const int64_t rbase = mat_off + row * ldc + col0;
-          const uint4* xp = reinterpret_cast<const uint4*>(aux + rbase);
-          float f[32];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xp[q], f + 8 * q);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
-          if (a.stage == kGemmBX) {
-            uint4* op = reinterpret_cast<uint4*>(out + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) op[q] = Vec16<T>::pack(f + 8 * q);
-          } else if (row < a.m) {
-            const FinalLeaf& L = a.final_leaf[fl];
-            const int64_t bi = g - L.group_mat_begin;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
-            if (!L.transposed && L.vec_ok && col0 + 32 <= a.n) {
-              final_store32(a, L, bi, row, col0, f);
-            } else {
-              // Transposed leaves: lanes hold consecutive rows, so each
-              // scalar store is coalesced across the warp.
-#pragma unroll
-              for (int k = 0; k < 32; ++k) {
-                const int64_t c = col0 + k;
-                if (c < a.n) final_store(a, L, bi, row, c, f[k]);
-              }
-            }
-          }
-        }
+        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * BN + ch * 32, lane, fl, v, stg);
       }
       tc_fence_before();
       mbar_arrive(acce0 + 8 * acc);
@@ -488,7 +486,7 @@ constexpr int B_BYTES = BNH * BK * 2;    // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + tc::EPI_STAGE_BYTES;
 
 using tc::kTimeoutNs;
 using tc::smem_u32;
@@ -504,6 +502,7 @@ using tc::tmem_ld32;
 using tc::Vec16;
 using tc::lane16;
 using tc::record_error;
+using tc::epilogue_chunk;
 
 struct Tc2Params {
   NsGemmArgs a;
@@ -590,6 +589,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   // [0,S) full (leader), [S,2S) empty, [2S,2S+2) acc full, [2S+2,2S+4) acc empty (leader)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 4 x 32x33 floats
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -729,13 +729,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- Epilogue (warps 2..5 of both CTAs) ----------------
     const int quarter = warp & 3;
-    const int row_local = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const T* aux = static_cast<const T*>(a.aux);
-    T* out = static_cast<T*>(a.out);
-    const bool sym = P.sym;
-    const int64_t ldc = sym ? a.mp : a.np;
+    float* stg = epi_stage + (warp - 2) * (32 * 33);
     for (int64_t t = pair; t < P.total_tiles; t += npairs) {
       int64_t g;
       int I, J;
@@ -745,75 +741,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = int64_t(I) * 256 + int64_t(rank) * BM + row_local;
-      const int64_t mat_off = g * a.mp * ldc;
+      const int64_t row0 = int64_t(I) * 256 + int64_t(rank) * BM + quarter * 32;
       int fl = 0;
       if (a.stage == kGemmBXFinal) fl = find_final_leaf(a, g);
       for (int ch = 0; ch < 256 / 32; ++ch) {
         float v[32];
         __syncwarp();
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * 256 + ch * 32), v);
-        const int64_t col0 = int64_t(J) * 256 + ch * 32;
-        if (sym) {
-          if (col0 + 31 < row) continue;
-          const int64_t rbase = mat_off + row * ldc + col0;
-          float f[32];
-          if (a.stage == kSyrkPoly) {
-            const uint4* ap = reinterpret_cast<const uint4*>(aux + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) Vec16<T>::unpack(ap[q], f + 8 * q);
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] = a.alpha * v[k];
-          }
-          uint4 packed[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
-          uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
-          if (col0 >= row) {
-            uint4* op = reinterpret_cast<uint4*>(out + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) op[q] = packed[q];
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (col0 + k >= row) out16[rbase + k] = lane16(packed, k);
-          }
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int64_t c = col0 + k;
-            if (c > row) out16[mat_off + c * ldc + row] = lane16(packed, k);
-          }
-        } else {
-          const int64_t rbase = mat_off + row * ldc + col0;
-          const uint4* xp = reinterpret_cast<const uint4*>(aux + rbase);
-          float f[32];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xp[q], f + 8 * q);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
-          if (a.stage == kGemmBX) {
-            uint4* op = reinterpret_cast<uint4*>(out + rbase);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) op[q] = Vec16<T>::pack(f + 8 * q);
-          } else if (row < a.m) {
-            const FinalLeaf& L = a.final_leaf[fl];
-            const int64_t bi = g - L.group_mat_begin;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
-            if (!L.transposed && L.vec_ok && col0 + 32 <= a.n) {
-              final_store32(a, L, bi, row, col0, f);
-            } else {
-#pragma unroll
-              for (int k = 0; k < 32; ++k) {
-                const int64_t c = col0 + k;
-                if (c < a.n) final_store(a, L, bi, row, c, f[k]);
-              }
-            }
-          }
-        }
+        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * 256 + ch * 32, lane, fl, v, stg);
       }
       tc_fence_before();
       __syncwarp();
