@@ -108,6 +108,24 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
                            int32_t n_coeff_rows, int32_t ns_steps, float eps, int32_t precision,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* rf_newton_schulz for callers that cannot allocate device memory (no
+ * counterpart in the reference).  Hosts such as an XLA FFI handler, whose
+ * framework has reserved the GPU for its own pool, or fixed-budget deployments
+ * that forbid allocation after start-up, cannot supply a workspace; this entry
+ * point takes it from a static device array of RF_NS_NOALLOC_MAX_WORKSPACE
+ * bytes that every GPU loading the library keeps until exit.  Problems whose
+ * rf_newton_schulz_workspace_size exceeds that are rejected with RF_EINVAL.
+ * All calls on a device share the array (nothing in it needs clearing: each
+ * call writes every byte it reads), so calls that overlap on the GPU race:
+ * keep them on one stream.  The first call on a device looks the array's
+ * address up (cudaGetSymbolAddress) and should come before any stream
+ * capture.  Never calls cudaMalloc / cudaFree. */
+#define RF_NS_NOALLOC_MAX_WORKSPACE ((size_t)32 << 20)
+rf_status rf_newton_schulz_noalloc(const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
+                                   int64_t batch, int64_t rows, int64_t cols, const float* coeffs,
+                                   int32_t n_coeff_rows, int32_t ns_steps, float eps, int32_t precision,
+                                   void* stream);
+
 /* Deferred tail for gathered orthogonalised leaves (multi-GPU path):
  * out = -lr * (shape_scale * O + decay * p), O read from `o` in leaf layout. */
 typedef struct rf_tail_leaf {

@@ -31,6 +31,7 @@ EXPORTED = (
     "rf_muon_direction",
     "rf_newton_schulz_workspace_size",
     "rf_newton_schulz",
+    "rf_newton_schulz_noalloc",
     "rf_muon_tail",
     "rf_adamw_update",
     "rf_last_error",
@@ -159,6 +160,8 @@ def load(path: str | None = None):
         lib.rf_newton_schulz_workspace_size.argtypes = [i64, i64, i64, i32, ctypes.POINTER(sz)]
         lib.rf_newton_schulz.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float), i32,
                                          i32, ctypes.c_float, i32, vp, sz, vp]
+        lib.rf_newton_schulz_noalloc.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float),
+                                                 i32, i32, ctypes.c_float, i32, vp]
         lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, vp]
         lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
         for name in EXPORTED:
