@@ -138,16 +138,12 @@ def make_plan(sizes: Sequence[int], costs: Sequence[int], world_size: int, n_buc
     return ShardPlan(owner, buckets, loads)
 
 
-def exchange_bucket(bucket: BucketPlan, rank: int, world_size: int, send: torch.Tensor, group,
-                    all_gather: Callable | None = None) -> torch.Tensor:
+def exchange_bucket(bucket: BucketPlan, world_size: int, send: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather one bucket's per-rank segments: returns [world * seg]."""
     import torch.distributed as dist
 
     recv = torch.empty(world_size * bucket.seg, dtype=send.dtype, device=send.device)
-    if all_gather is None:
-        dist.all_gather_into_tensor(recv, send, group=group)
-    else:
-        all_gather(recv, send)
+    dist.all_gather_into_tensor(recv, send, group=group)
     return recv
 
 
@@ -155,6 +151,29 @@ def leaf_view(bucket: BucketPlan, recv: torch.Tensor, leaf: int, numel: int) -> 
     r, off = bucket.offsets[leaf]
     base = r * bucket.seg + off
     return recv[base:base + numel]
+
+
+def run_buckets(plan: ShardPlan, rank: int, world_size: int, sizes: Sequence[int], dtype: torch.dtype,
+                device: torch.device, compute_owned: Callable, exchange: Callable) -> list:
+    """Drive the bucketed owner-computes / all-gather exchange.
+
+    For each bucket: allocate the send segment, ``compute_owned(leaf_ids,
+    offsets, send)`` writes this rank's owned leaves (``offsets[i]`` = element
+    offset of leaf i in ``send``), then ``exchange(bucket, send)`` returns the
+    gathered ``[world * seg]`` buffer.  Returns ``[(leaf, view)]`` for every
+    leaf, where ``view`` is that leaf's data inside its bucket's gathered
+    buffer.  Every rank makes the same sequence of ``exchange`` calls.
+    """
+    out = []
+    for b in plan.buckets:
+        send = torch.zeros(max(b.seg, 1), dtype=dtype, device=device)
+        mine = [i for i in b.leaves if plan.owner[i] == rank]
+        if mine:
+            compute_owned(mine, {i: b.offsets[i][1] for i in mine}, send)
+        recv = exchange(b, send[: b.seg])
+        for i in b.leaves:
+            out.append((i, leaf_view(b, recv, i, sizes[i])))
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -167,7 +186,7 @@ _O_DTYPE = {_lib.RF_NS_F16: torch.float16, _lib.RF_NS_BF16: torch.bfloat16, _lib
 def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float):
     """Sharded version of the fused Muon-branch update (see module doc)."""
     from .base import rf_dtype, run_tail, stream_handle
-    from .muon import _leaf_table
+    from .muon import _finish_leaves, _leaf_table
 
     if not ml:
         return []
@@ -187,41 +206,41 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         ctx.comm_stream = torch.cuda.Stream(device=dev)
     comm = ctx.comm_stream
     prm.fuse_tail = 0
-    recvs = []
-    for b in plan.buckets:
-        send = torch.empty(max(b.seg, 1), dtype=odt, device=dev)
-        mine = [i for i in b.leaves if plan.owner[i] == ctx.rank]
-        if mine:
-            sub = [ml[i] for i in mine]
-            arr = _leaf_table(sub, [1.0] * len(sub), [0.0] * len(sub))
-            for j, i in enumerate(mine):
-                off = b.offsets[i][1]
-                arr[j].out = send.data_ptr() + off * send.element_size()
-                arr[j].out_dtype = rf_dtype(send)
-            nbytes = ctypes.c_size_t()
-            _lib.check(lib.rf_muon_workspace_size(arr, len(sub), prm.precision, ctypes.byref(nbytes)))
-            ws = _runtime.workspace(dev, nbytes.value)
-            _lib.check(lib.rf_muon_update(arr, len(sub), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
-                                          stream_handle(ml[0].g)))
+
+    def compute_owned(ids, offsets, send):
+        # Momentum + NS for this rank's leaves of the bucket, O written (leaf
+        # layout, 16-bit) straight into their segment of the send buffer.
+        sub = [ml[i] for i in ids]
+        arr = _leaf_table(sub, [1.0] * len(sub), [0.0] * len(sub))
+        for j, i in enumerate(ids):
+            arr[j].out = send.data_ptr() + offsets[i] * send.element_size()
+            arr[j].out_dtype = rf_dtype(send)
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.rf_muon_workspace_size(arr, len(sub), prm.precision, ctypes.byref(nbytes)))
+        ws = _runtime.workspace(dev, nbytes.value)
+        _lib.check(lib.rf_muon_update(arr, len(sub), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
+                                      stream_handle(ml[0].g)))
+
+    def exchange(bucket, send):
+        # Gather on the side stream once this bucket's NS is done, while the
+        # compute stream moves on to the next bucket.
         ready = torch.cuda.Event()
         ready.record(compute)
         comm.wait_event(ready)
         with torch.cuda.stream(comm):
-            recv = exchange_bucket(b, ctx.rank, ctx.world_size, send[: b.seg] if b.seg else send[:0], ctx.group)
-            send.record_stream(comm)
-            recv.record_stream(comm)
-        recvs.append(recv)
+            recv = exchange_bucket(bucket, ctx.world_size, send, ctx.group)
+        send.record_stream(comm)
+        recv.record_stream(compute)
+        return recv
+
+    views = run_buckets(plan, ctx.rank, ctx.world_size, sizes, odt, dev, compute_owned, exchange)
     done = torch.cuda.Event()
     done.record(comm)
     compute.wait_event(done)
     items = []
-    for b, recv in zip(plan.buckets, recvs):
-        for i in b.leaves:
-            L = ml[i]
-            o = leaf_view(b, recv, i, sizes[i])
-            p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
-            items.append((o, p, L.out.view(-1), scales[i], decays[i]))
+    for i, o in views:
+        L = ml[i]
+        p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+        items.append((o, p, L.out.view(-1), scales[i], decays[i]))
     run_tail(items, lr)
-    from .muon import _finish_leaves
-
     return _finish_leaves(ml)

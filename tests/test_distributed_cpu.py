@@ -1,0 +1,113 @@
+"""Multi-GPU host logic on CPU: leaf ownership (LPT on NS FLOPs), bucket
+layout, and the bucketed owner-computes / all-gather exchange over world-size-2
+gloo process groups."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+from rollfast_b200.distributed import lpt_assign, make_plan, ns_flops, run_buckets
+
+
+def llama_leaves():
+    layer = [(4096, 4096), (4096, 1024), (4096, 1024), (4096, 4096), (4096, 14336), (4096, 14336), (14336, 4096)]
+    return [s for _ in range(32) for s in layer]
+
+
+def test_ns_flops_counts_the_smaller_side_as_m():
+    assert ns_flops(1, 4096, 14336) == 4 * 4096 ** 2 * 14336 + 2 * 4096 ** 3
+    assert ns_flops(2, 14336, 4096) == 2 * ns_flops(1, 4096, 14336)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_lpt_balances_llama_leaves_exactly(world):
+    leaves = llama_leaves()
+    costs = [ns_flops(1, *s) for s in leaves]
+    owner = lpt_assign(costs, world)
+    loads = [0] * world
+    for c, r in zip(costs, owner):
+        loads[r] += c
+    assert max(loads) == min(loads)  # 96 / 64 / 64 leaves of three costs divide evenly
+    assert sorted(set(owner)) == list(range(world))
+
+
+def test_lpt_is_deterministic_and_bounded():
+    costs = [7, 7, 5, 3, 3, 2, 1, 1]
+    a = lpt_assign(costs, 3)
+    assert a == lpt_assign(costs, 3)
+    loads = [sum(c for c, r in zip(costs, a) if r == k) for k in range(3)]
+    assert max(loads) <= sum(costs) / 3 + max(costs)
+
+
+@pytest.mark.parametrize("world,buckets", [(2, 1), (2, 4), (8, 4), (3, 3)])
+def test_bucket_layout_covers_every_leaf_once(world, buckets):
+    leaves = llama_leaves()
+    sizes = [a * b for a, b in leaves]
+    costs = [ns_flops(1, *s) for s in leaves]
+    plan = make_plan(sizes, costs, world, buckets)
+    seen = [i for b in plan.buckets for i in b.leaves]
+    assert seen == list(range(len(leaves)))
+    assert len(plan.buckets) <= buckets
+    for b in plan.buckets:
+        used = [0] * world
+        for i in b.leaves:
+            r, off = b.offsets[i]
+            assert r == plan.owner[i] and off == used[r]
+            used[r] += sizes[i]
+        assert b.seg == max(used)
+    if len(plan.buckets) > 1:  # cost shares shrink towards the end
+        bc = [sum(costs[i] for i in b.leaves) for b in plan.buckets]
+        assert bc[-1] < bc[0]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _exchange_worker(rank, world, port, sizes, costs, buckets, q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = make_plan(sizes, costs, world, buckets)
+
+        def compute_owned(ids, offsets, send):
+            for i in ids:  # stand-in for the NS output of leaf i, computed by its owner
+                send[offsets[i]: offsets[i] + sizes[i]] = torch.arange(sizes[i], dtype=torch.float32) + 1000.0 * i
+
+        def exchange(bucket, send):
+            recv = torch.empty(world * bucket.seg, dtype=send.dtype)
+            dist.all_gather_into_tensor(recv, send)
+            return recv
+
+        views = run_buckets(plan, rank, world, sizes, torch.float32, torch.device("cpu"), compute_owned, exchange)
+        ok = sorted(i for i, _ in views) == list(range(len(sizes)))
+        for i, v in views:
+            ok &= bool(torch.equal(v, torch.arange(sizes[i], dtype=torch.float32) + 1000.0 * i))
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("buckets", [1, 3])
+def test_gloo_world2_owner_compute_and_all_gather(buckets):
+    import torch.multiprocessing as mp
+
+    sizes = [96, 40, 40, 96, 300, 300, 300, 17, 5]
+    costs = [ns_flops(1, 8, s // 8 if s % 8 == 0 else s) for s in sizes]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, sizes, costs, buckets, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: True, 1: True}

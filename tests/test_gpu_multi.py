@@ -1,0 +1,82 @@
+"""Sharded Muon on 2 GPUs (NCCL): leaf ownership + all-gather must give the
+same updates as the unsharded single-GPU path.  Runs as child processes and
+needs >= 2 GPUs (skipped otherwise)."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tree(dev, seed):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    shapes = {"q": (512, 512), "k": (512, 128), "v": (512, 128), "up": (512, 1536), "down": (1536, 512),
+              "stack": (3, 256, 768), "norm": (512,)}
+    return {k: torch.randn(s, device=dev, generator=g).to(torch.bfloat16) for k, s in shapes.items()}
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import rollfast_b200 as rf
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        params = {k: (v.float() * 0.02).to(torch.bfloat16) for k, v in _tree(dev, 1).items()}
+        specs = {k: (rf.MatrixDimensionNumbers(1, 2) if v.ndim == 3 else
+                     (rf.MatrixDimensionNumbers() if v.ndim == 2 else None)) for k, v in params.items()}
+        kw = dict(learning_rate=0.02, weight_decay=0.01, muon_weight_dimension_numbers=specs)
+        ref_tx, sh_tx = rf.muon(**kw), rf.muon(**kw)
+        ref_st, sh_st = ref_tx.init(params), sh_tx.init(params)
+        ok = True
+        for step in range(2):
+            grads = _tree(dev, 10 + step)
+            rf.distributed.clear()
+            u_ref, ref_st = ref_tx.update(grads, ref_st, params)
+            rf.distributed.configure(buckets=2)
+            u_sh, sh_st = sh_tx.update(grads, sh_st, params)
+            rf.distributed.clear()
+            torch.cuda.synchronize()
+            for k in params:
+                e = float(torch.linalg.vector_norm(u_sh[k] - u_ref[k]) / torch.linalg.vector_norm(u_ref[k]))
+                ok &= e <= 2e-3  # 16-bit gathered O vs fused fp32 O
+        q.put((rank, ok))
+    except Exception as exc:  # report instead of hanging the other rank
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_update_matches_single_gpu_on_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: True, 1: True}, results
