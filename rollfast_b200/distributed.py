@@ -138,13 +138,11 @@ def make_plan(sizes: Sequence[int], costs: Sequence[int], world_size: int, n_buc
     return ShardPlan(owner, buckets, loads)
 
 
-def exchange_bucket(bucket: BucketPlan, world_size: int, send: torch.Tensor, group=None) -> torch.Tensor:
-    """All-gather one bucket's per-rank segments: returns [world * seg]."""
+def exchange_bucket(send: torch.Tensor, recv: torch.Tensor, group=None) -> None:
+    """All-gather one bucket's per-rank segments into recv ([world * seg])."""
     import torch.distributed as dist
 
-    recv = torch.empty(world_size * bucket.seg, dtype=send.dtype, device=send.device)
     dist.all_gather_into_tensor(recv, send, group=group)
-    return recv
 
 
 def leaf_view(bucket: BucketPlan, recv: torch.Tensor, leaf: int, numel: int) -> torch.Tensor:
@@ -153,27 +151,34 @@ def leaf_view(bucket: BucketPlan, recv: torch.Tensor, leaf: int, numel: int) -> 
     return recv[base:base + numel]
 
 
-def run_buckets(plan: ShardPlan, rank: int, world_size: int, sizes: Sequence[int], dtype: torch.dtype,
-                device: torch.device, compute_owned: Callable, exchange: Callable) -> list:
+def run_buckets(plan: ShardPlan, rank: int, world_size: int, sizes: Sequence[int], compute_owned: Callable,
+                exchange: Callable, buffers: list) -> list:
     """Drive the bucketed owner-computes / all-gather exchange.
 
-    For each bucket: allocate the send segment, ``compute_owned(leaf_ids,
-    offsets, send)`` writes this rank's owned leaves (``offsets[i]`` = element
-    offset of leaf i in ``send``), then ``exchange(bucket, send)`` returns the
-    gathered ``[world * seg]`` buffer.  Returns ``[(leaf, view)]`` for every
-    leaf, where ``view`` is that leaf's data inside its bucket's gathered
-    buffer.  Every rank makes the same sequence of ``exchange`` calls.
+    ``buffers[k] = (send, recv)`` for bucket k (``send`` holds ``seg``
+    elements, ``recv`` ``world * seg``).  For each bucket,
+    ``compute_owned(leaf_ids, offsets, send)`` writes this rank's owned leaves
+    (``offsets[i]`` = element offset of leaf i in ``send``), then
+    ``exchange(bucket, send, recv)`` gathers every rank's segment into
+    ``recv``.  Returns ``[(leaf, view)]`` for every leaf, ``view`` being its
+    data in the gathered buffer.  Every rank makes the same sequence of
+    ``exchange`` calls.
     """
     out = []
-    for b in plan.buckets:
-        send = torch.zeros(max(b.seg, 1), dtype=dtype, device=device)
+    for b, (send, recv) in zip(plan.buckets, buffers):
         mine = [i for i in b.leaves if plan.owner[i] == rank]
         if mine:
             compute_owned(mine, {i: b.offsets[i][1] for i in mine}, send)
-        recv = exchange(b, send[: b.seg])
+        exchange(b, send, recv)
         for i in b.leaves:
             out.append((i, leaf_view(b, recv, i, sizes[i])))
     return out
+
+
+def bucket_buffers(plan: ShardPlan, world_size: int, dtype: torch.dtype, device: torch.device) -> list:
+    """Persistent (send, recv) pairs, one per bucket, reused every step."""
+    return [(torch.empty(max(b.seg, 1), dtype=dtype, device=device)[: b.seg],
+             torch.empty(world_size * b.seg, dtype=dtype, device=device)) for b in plan.buckets]
 
 
 # ---------------------------------------------------------------------------
@@ -192,14 +197,20 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         return []
     dev = ml[0].g.device
     sizes = [L.out.numel() for L in ml]
-    key = tuple((L.layout.flat_shape, L.g.dtype) for L in ml)
-    plan = ctx.plans.get(key)
-    if plan is None:
+    odt = _O_DTYPE[prm.precision]
+    key = (tuple((L.layout.flat_shape, L.g.dtype) for L in ml), odt, dev)
+    entry = ctx.plans.get(key)
+    if entry is None:
         steps = prm.n_coeff_rows or prm.ns_steps
         costs = [ns_flops(*L.layout.flat_shape) * steps for L in ml]
         plan = make_plan(sizes, costs, ctx.world_size, ctx.buckets)
-        ctx.plans[key] = plan
-    odt = _O_DTYPE[prm.precision]
+        # Stream order makes reuse safe: a bucket's send buffer is rewritten
+        # only after the compute stream waited for the previous step's
+        # gathers, and its recv buffer is regathered only after this step's
+        # tail (compute stream) has read it.
+        entry = (plan, bucket_buffers(plan, ctx.world_size, odt, dev))
+        ctx.plans[key] = entry
+    plan, buffers = entry
     lib = _lib.load()
     compute = torch.cuda.current_stream(dev)
     if ctx.comm_stream is None:
@@ -221,19 +232,16 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         _lib.check(lib.rf_muon_update(arr, len(sub), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
                                       stream_handle(ml[0].g)))
 
-    def exchange(bucket, send):
+    def exchange(bucket, send, recv):
         # Gather on the side stream once this bucket's NS is done, while the
         # compute stream moves on to the next bucket.
         ready = torch.cuda.Event()
         ready.record(compute)
         comm.wait_event(ready)
         with torch.cuda.stream(comm):
-            recv = exchange_bucket(bucket, ctx.world_size, send, ctx.group)
-        send.record_stream(comm)
-        recv.record_stream(compute)
-        return recv
+            exchange_bucket(send, recv, ctx.group)
 
-    views = run_buckets(plan, ctx.rank, ctx.world_size, sizes, odt, dev, compute_owned, exchange)
+    views = run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
     done = torch.cuda.Event()
     done.record(comm)
     compute.wait_event(done)

@@ -8,7 +8,7 @@ import socket
 import pytest
 import torch
 
-from rollfast_b200.distributed import lpt_assign, make_plan, ns_flops, run_buckets
+from rollfast_b200.distributed import bucket_buffers, lpt_assign, make_plan, ns_flops, run_buckets
 
 
 def llama_leaves():
@@ -81,12 +81,13 @@ def _exchange_worker(rank, world, port, sizes, costs, buckets, q):
             for i in ids:  # stand-in for the NS output of leaf i, computed by its owner
                 send[offsets[i]: offsets[i] + sizes[i]] = torch.arange(sizes[i], dtype=torch.float32) + 1000.0 * i
 
-        def exchange(bucket, send):
-            recv = torch.empty(world * bucket.seg, dtype=send.dtype)
+        def exchange(bucket, send, recv):
             dist.all_gather_into_tensor(recv, send)
-            return recv
 
-        views = run_buckets(plan, rank, world, sizes, torch.float32, torch.device("cpu"), compute_owned, exchange)
+        buffers = bucket_buffers(plan, world, torch.float32, torch.device("cpu"))
+        views = []
+        for _ in range(2):  # persistent buffers reused on a second step
+            views = run_buckets(plan, rank, world, sizes, compute_owned, exchange, buffers)
         ok = sorted(i for i, _ in views) == list(range(len(sizes)))
         for i, v in views:
             ok &= bool(torch.equal(v, torch.arange(sizes[i], dtype=torch.float32) + 1000.0 * i))
