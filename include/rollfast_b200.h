@@ -80,11 +80,22 @@ typedef struct rf_muon_params {
   int32_t precision;     /* rf_ns_precision */
   float lr;              /* learning rate at this step (scale_by_learning_rate) */
   int32_t fuse_tail;     /* 1: out = -lr*(scale*O + decay*p); 0: out = O (leaf layout) */
+  /* Optional second stream (NULL: everything on `stream`).  The HBM-bound
+   * preparation of the next shape sub-batch (momentum, norms, operand load)
+   * then runs on it while the current sub-batch's Newton-Schulz GEMMs run on
+   * `stream`; ordering is kept with events and all work is ordered before
+   * later work on `stream` when the call returns.  Needs a workspace sized
+   * with pipelined = 1. */
+  void* aux_stream;
+  /* SMs the GEMM kernels leave free for concurrent kernels (e.g. a
+   * collective or the tail on another stream); 0 = use every SM. */
+  int32_t reserve_sms;
 } rf_muon_params;
 
-/* Bytes of workspace rf_muon_update needs for these leaves and precision. */
+/* Bytes of workspace rf_muon_update needs for these leaves and precision
+ * (pipelined != 0: two sub-batch regions, for use with an aux stream). */
 rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision,
-                                 size_t* bytes);
+                                 int32_t pipelined, size_t* bytes);
 
 /* Full Muon-branch step for n_leaves leaves: momentum (EMA / heavy-ball,
  * Nesterov, bias correction), Frobenius normalisation, quintic Newton-Schulz,

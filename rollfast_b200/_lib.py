@@ -74,6 +74,8 @@ class RfMuonParams(ctypes.Structure):
         ("precision", ctypes.c_int32),
         ("lr", ctypes.c_float),
         ("fuse_tail", ctypes.c_int32),
+        ("aux_stream", ctypes.c_void_p),
+        ("reserve_sms", ctypes.c_int32),
     ]
 
 
@@ -154,7 +156,7 @@ def load(path: str | None = None):
         lib.rf_profile_begin.argtypes = []
         lib.rf_profile_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
-        lib.rf_muon_workspace_size.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, i32, ctypes.POINTER(sz)]
+        lib.rf_muon_workspace_size.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, i32, i32, ctypes.POINTER(sz)]
         lib.rf_muon_update.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, ctypes.POINTER(RfMuonParams), vp, sz, vp]
         lib.rf_muon_direction.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, ctypes.POINTER(RfMuonParams), vp]
         lib.rf_newton_schulz_workspace_size.argtypes = [i64, i64, i64, i32, ctypes.POINTER(sz)]

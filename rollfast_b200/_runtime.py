@@ -44,6 +44,26 @@ def ns_precision_name(p: int | None = None) -> str:
     return {_lib.RF_NS_F16: "f16", _lib.RF_NS_BF16: "bf16", _lib.RF_NS_F32: "f32"}[p]
 
 
+_aux_streams: dict = {}
+
+
+def pipelined() -> bool:
+    """Overlap HBM-bound preparation / AdamW with the Newton-Schulz GEMMs on
+    a second stream (ROLLFAST_PIPELINE=0 turns it off)."""
+    return os.environ.get("ROLLFAST_PIPELINE", "1") != "0"
+
+
+def aux_stream(device: torch.device) -> torch.cuda.Stream:
+    """The persistent second stream of ``device``."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _lock:
+        s = _aux_streams.get(idx)
+        if s is None:
+            s = torch.cuda.Stream(device=torch.device("cuda", idx))
+            _aux_streams[idx] = s
+        return s
+
+
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """A device buffer of at least ``nbytes`` for the current stream."""
     stream = torch.cuda.current_stream(device)

@@ -107,7 +107,8 @@ struct Plan {
   int64_t total_mats = 0;
   int64_t total_chunks = 0;
   size_t off_partials = 0, off_scale = 0, off_ns = 0, bytes = 0;
-  size_t ns_bytes = 0;  // max over sub-batches
+  size_t ns_bytes = 0;  // one region: max over sub-batches
+  int regions = 1;      // 2 when pipelined on an aux stream
   int precision = RF_NS_F16;
 };
 
@@ -115,7 +116,7 @@ static size_t ns_elem(int precision) { return precision == RF_NS_F32 ? 4 : 2; }
 
 static int64_t chunks_per_mat(int64_t numel) { return ceil_div(numel, kChunk); }
 
-static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan& P) {
+static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan& P, int regions = 1) {
   if (precision != RF_NS_F16 && precision != RF_NS_BF16 && precision != RF_NS_F32)
     return fail(RF_EINVAL, "unknown NS precision");
   P.precision = precision;
@@ -159,10 +160,11 @@ static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan
       P.ns_bytes = std::max(P.ns_bytes, 2 * x + 2 * a);
     }
   }
+  P.regions = regions;
   P.off_partials = 0;
   P.off_scale = align_up(size_t(P.total_chunks) * 4, 1024);
   P.off_ns = P.off_scale + align_up(size_t(P.total_mats) * 4, 1024);
-  P.bytes = P.off_ns + P.ns_bytes;
+  P.bytes = P.off_ns + size_t(regions) * P.ns_bytes;
   return RF_OK;
 }
 
@@ -177,35 +179,23 @@ static rf_status validate_leaf(const rf_muon_leaf& l, int i, bool need_out) {
   return RF_OK;
 }
 
-// Runs steps 1-3 for the leaves of `P` (all have NS work).
-static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
-                              int ns_steps, float eps, int fuse_tail, float lr, void* ws, size_t ws_bytes,
-                              cudaStream_t st) {
-  if (P.leaves.empty()) return RF_OK;
-  if (!ws || ws_bytes < P.bytes)
-    return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
-                               std::to_string(ws_bytes));
-  if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(RF_EINVAL, "workspace must be 256-byte aligned");
-  uint8_t* base = static_cast<uint8_t*>(ws);
-  float* partials = reinterpret_cast<float*>(base + P.off_partials);
-  float* denom = reinterpret_cast<float*>(base + P.off_scale);
-  uint8_t* ns = base + P.off_ns;
-
-  // --- 1+2: momentum / sum of squares, then per-matrix denominators -------
-  // Each launch takes leaves of one grad dtype and its own contiguous range
-  // of partial sums.
-  int64_t chunk_cursor = 0;
+// Launches the momentum pass (sum of squares) and the per-matrix norm for
+// the leaves `ids` of one sub-batch; `chunk_base` is the first partial-sum
+// slot this sub-batch owns.
+static rf_status prepare_norms(const Plan& P, const std::vector<int>& ids, const MomentumCoeffs& mc, float* partials,
+                               int64_t chunk_base, float* denom, float eps, cudaStream_t st) {
+  int64_t cursor = chunk_base;
   for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
-    std::vector<int> ids;
-    for (size_t i = 0; i < P.leaves.size(); ++i)
-      if (P.leaves[i].gdt == gdt) ids.push_back(int(i));
-    for (size_t s = 0; s < ids.size(); s += kMaxLeavesPerLaunch) {
+    std::vector<int> sel;
+    for (int i : ids)
+      if (P.leaves[i].gdt == gdt) sel.push_back(i);
+    for (size_t s = 0; s < sel.size(); s += kMaxLeavesPerLaunch) {
       MomentumLaunch L{};
       L.c = mc;
-      L.partials = partials + chunk_cursor;
+      L.partials = partials + cursor;
       int64_t chunks = 0, mats = 0;
-      for (size_t k = s; k < std::min(ids.size(), s + size_t(kMaxLeavesPerLaunch)); ++k) {
-        const LeafPlan& lp = P.leaves[ids[k]];
+      for (size_t k = s; k < std::min(sel.size(), s + size_t(kMaxLeavesPerLaunch)); ++k) {
+        const LeafPlan& lp = P.leaves[sel[k]];
         MomentumLeaf& ml = L.leaf[L.n++];
         ml.g = lp.g;
         ml.mu = lp.mu;
@@ -222,25 +212,81 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       }
       L.total_chunks = chunks;
       L.total_mats = mats;
-      chunk_cursor += chunks;
+      cursor += chunks;
       RF_TRY(launch_momentum_sumsq(L, gdt, st));
       RF_TRY(launch_norm_finalize(L, denom, eps, st));
     }
   }
+  return RF_OK;
+}
 
-  // --- 3: per shape group, per sub-batch: load + NS iterations -------------
+// RAII set of events (host objects; no device memory).
+struct EventPool {
+  std::vector<cudaEvent_t> ev;
+  ~EventPool() {
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+  }
+  rf_status get(cudaEvent_t* out) {
+    cudaEvent_t e;
+    cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (err != cudaSuccess) return fail(RF_ECUDA, std::string("cudaEventCreate: ") + cudaGetErrorString(err));
+    ev.push_back(e);
+    *out = e;
+    return RF_OK;
+  }
+};
+
+// Runs the Muon pipeline for the leaves of `P` (all have NS work), one shape
+// sub-batch after another.  Per sub-batch: momentum + norms + operand load
+// (HBM-bound, on `aux` when given, else on `st`) and ns_steps x 3 GEMM stages
+// on `st`.  With `aux`, sub-batch k+1's preparation overlaps sub-batch k's
+// GEMMs; workspace regions alternate, so preparing k+2 waits for k's GEMMs.
+static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
+                              int ns_steps, float eps, int fuse_tail, float lr, int reserve_sms, void* ws,
+                              size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
+  if (P.leaves.empty()) return RF_OK;
+  if (!ws || ws_bytes < P.bytes)
+    return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
+                               std::to_string(ws_bytes));
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(RF_EINVAL, "workspace must be 256-byte aligned");
+  if (aux && P.regions < 2) return fail(RF_EINVAL, "an aux stream needs a workspace sized with pipelined = 1");
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  float* partials = reinterpret_cast<float*>(base + P.off_partials);
+  float* denom = reinterpret_cast<float*>(base + P.off_scale);
+  const cudaStream_t prep = aux ? aux : st;
   const size_t es = ns_elem(P.precision);
+  EventPool events;
+  cudaEvent_t start_ev = nullptr;
+  if (aux) {
+    // The aux stream starts after everything already queued on `st`.
+    RF_TRY(events.get(&start_ev));
+    cudaEventRecord(start_ev, st);
+    cudaStreamWaitEvent(aux, start_ev, 0);
+  }
+  std::vector<cudaEvent_t> done;  // per sub-batch: its GEMMs finished (on st)
+  int64_t chunk_base = 0;
+  int k = 0;
   for (const GroupPlan& gp : P.groups) {
     const NsScales sc = ns_scales(gp.m, P.precision);
     for (const auto& sub : gp.subs) {
-      int64_t G = 0;
-      for (int li : sub) G += P.leaves[li].batch;
+      const int region = aux ? (k & 1) : 0;
+      uint8_t* ns = base + P.off_ns + size_t(region) * P.ns_bytes;
+      int64_t G = 0, sub_chunks = 0;
+      for (int li : sub) {
+        G += P.leaves[li].batch;
+        sub_chunks += P.leaves[li].batch * chunks_per_mat(P.leaves[li].rows * P.leaves[li].cols);
+      }
       const size_t xbytes = align_up(size_t(G) * gp.mp * gp.np * es, 1024);
       const size_t abytes = align_up(size_t(G) * gp.mp * gp.mp * es, 1024);
       uint8_t* X0 = ns;
       uint8_t* X1 = ns + xbytes;
       uint8_t* Am = ns + 2 * xbytes;
       uint8_t* Bm = Am + abytes;
+
+      // ---- preparation: momentum, norms, operand load ----
+      if (aux && k >= 2) cudaStreamWaitEvent(aux, done[k - 2], 0);  // region reuse
+      RF_TRY(prepare_norms(P, sub, mc, partials, chunk_base, denom, eps, prep));
+      chunk_base += sub_chunks;
 
       LoadLaunch ld{};
       ld.c = mc;
@@ -252,6 +298,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       ld.group_mats = G;
       NsGemmArgs ga{};
       ga.precision = P.precision;
+      ga.reserve_sms = reserve_sms;
       ga.G = G;
       ga.m = gp.m;
       ga.n = gp.n;
@@ -292,9 +339,16 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
         bool any = false;
         for (int li : sub) any |= P.leaves[li].gdt == gdt;
-        if (any) RF_TRY(launch_ns_load(ld, gdt, P.precision, st));
+        if (any) RF_TRY(launch_ns_load(ld, gdt, P.precision, prep));
+      }
+      if (aux) {
+        cudaEvent_t ready;
+        RF_TRY(events.get(&ready));
+        cudaEventRecord(ready, aux);
+        cudaStreamWaitEvent(st, ready, 0);
       }
 
+      // ---- Newton-Schulz GEMM stages on st ----
       uint8_t* xc = X0;
       uint8_t* xn = X1;
       for (int it = 0; it < ns_steps; ++it) {
@@ -325,6 +379,13 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         RF_TRY(launch_ns_gemm(ga, st));
         std::swap(xc, xn);
       }
+      if (aux) {
+        cudaEvent_t fin;
+        RF_TRY(events.get(&fin));
+        cudaEventRecord(fin, st);
+        done.push_back(fin);
+      }
+      ++k;
     }
   }
   return RF_OK;
@@ -393,12 +454,13 @@ rf_status rf_sync_check(void* stream) {
   return take_device_error();
 }
 
-rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision, size_t* bytes) {
+rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision, int32_t pipelined,
+                                 size_t* bytes) {
   if (!bytes) return fail(RF_EINVAL, "null output pointer");
   std::vector<LeafPlan> lp;
   RF_TRY(leaves_from_abi(leaves, n_leaves, lp, false));
   Plan P;
-  RF_TRY(build_plan(lp, precision, P));
+  RF_TRY(build_plan(lp, precision, P, pipelined ? 2 : 1));
   *bytes = P.bytes;
   return RF_OK;
 }
@@ -414,12 +476,14 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
   int iters = 0;
   RF_TRY(check_coeffs(p.coeffs, p.n_coeff_rows, p.ns_steps, &iters));
+  if (p.reserve_sms < 0) return fail(RF_EINVAL, "reserve_sms must be >= 0");
   std::vector<LeafPlan> lp;
   RF_TRY(leaves_from_abi(leaves, n_leaves, lp, true));
   Plan P;
-  RF_TRY(build_plan(lp, p.precision, P));
+  RF_TRY(build_plan(lp, p.precision, P, p.aux_stream ? 2 : 1));
   return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.fuse_tail, p.lr,
-                      workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                      p.reserve_sms, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                      static_cast<cudaStream_t>(p.aux_stream));
 }
 
 rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
@@ -503,8 +567,8 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
   RF_TRY(ns_plan(batch, rows, cols, precision, P, x, x_dtype, out, out_dtype));
   MomentumCoeffs mc{};
   mc.mode = kDirIdentity;
-  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, 0, 0.f, workspace, workspace_bytes,
-                      static_cast<cudaStream_t>(stream));
+  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, 0, 0.f, 0, workspace, workspace_bytes,
+                      static_cast<cudaStream_t>(stream), nullptr);
 }
 
 rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, void* stream) {

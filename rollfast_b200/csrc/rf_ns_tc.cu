@@ -834,7 +834,9 @@ rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
   if (sym) RF_TRY(make_map(&mB, a.b_op, a.precision, a.G, a.mp, K, BN));
   else RF_TRY(make_map(&mB, a.b_op, a.precision, a.G, a.mp, a.np, 64));
 
-  const int64_t grid = P.total_tiles < num_sms() ? P.total_tiles : num_sms();
+  int64_t cap = num_sms() - a.reserve_sms;
+  if (cap < 1) cap = 1;
+  const int64_t grid = P.total_tiles < cap ? P.total_tiles : cap;
   k_ns_tc<T><<<unsigned(grid), NUM_THREADS, SMEM_BYTES, st>>>(mA, mB, P);
   return check_launch("k_ns_tc");
 }
@@ -880,7 +882,9 @@ rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
     }
     return int64_t(n);
   }();
-  const int64_t pairs = P.total_tiles < pairs_max ? P.total_tiles : pairs_max;
+  int64_t cap = pairs_max - (a.reserve_sms + 1) / 2;
+  if (cap < 1) cap = 1;
+  const int64_t pairs = P.total_tiles < cap ? P.total_tiles : cap;
   k_ns_tc2<T><<<unsigned(2 * pairs), NUM_THREADS, SMEM_BYTES, st>>>(mA, mB, P);
   return check_launch("k_ns_tc2");
 }

@@ -37,19 +37,24 @@ class ShardContext:
     world_size: int
     group: object = None
     buckets: int = 4
+    reserve_sms: int = 16
     plans: dict = field(default_factory=dict)
     comm_stream: object = None
 
 
-def configure(group=None, *, buckets: int = 4) -> ShardContext:
-    """Enable sharded Muon updates over ``group`` (default: the world group)."""
+def configure(group=None, *, buckets: int = 4, reserve_sms: int = 16) -> ShardContext:
+    """Enable sharded Muon updates over ``group`` (default: the world group).
+
+    ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
+    all-gather (NCCL) and the per-bucket tail run beside it.
+    """
     import torch.distributed as dist
 
     global _ctx
     if not dist.is_initialized():
         raise RuntimeError("torch.distributed must be initialised before rollfast_b200.distributed.configure")
     _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
-                        buckets=max(1, int(buckets)))
+                        buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)))
     return _ctx
 
 
@@ -190,8 +195,8 @@ _O_DTYPE = {_lib.RF_NS_F16: torch.float16, _lib.RF_NS_BF16: torch.bfloat16, _lib
 
 def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float):
     """Sharded version of the fused Muon-branch update (see module doc)."""
-    from .base import rf_dtype, run_tail, stream_handle
-    from .muon import _finish_leaves, _leaf_table
+    from .base import rf_dtype, run_tail
+    from .muon import _finish_leaves, _leaf_table, run_muon_table
 
     if not ml:
         return []
@@ -226,29 +231,28 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         for j, i in enumerate(ids):
             arr[j].out = send.data_ptr() + offsets[i] * send.element_size()
             arr[j].out_dtype = rf_dtype(send)
-        nbytes = ctypes.c_size_t()
-        _lib.check(lib.rf_muon_workspace_size(arr, len(sub), prm.precision, ctypes.byref(nbytes)))
-        ws = _runtime.workspace(dev, nbytes.value)
-        _lib.check(lib.rf_muon_update(arr, len(sub), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
-                                      stream_handle(ml[0].g)))
+        run_muon_table(arr, len(sub), prm, dev)
 
     def exchange(bucket, send, recv):
         # Gather on the side stream once this bucket's NS is done, while the
-        # compute stream moves on to the next bucket.
+        # compute stream moves on to the next bucket; the bucket's tail
+        # (-lr (shape O + decay p) for all its leaves) follows on the same
+        # stream, beside the next bucket's GEMMs.
         ready = torch.cuda.Event()
         ready.record(compute)
         comm.wait_event(ready)
         with torch.cuda.stream(comm):
             exchange_bucket(send, recv, ctx.group)
+            items = []
+            for i in bucket.leaves:
+                L = ml[i]
+                o = leaf_view(bucket, recv, i, sizes[i])
+                p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+                items.append((o, p, L.out.view(-1), scales[i], decays[i]))
+            run_tail(items, lr)
 
-    views = run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
+    run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
     done = torch.cuda.Event()
     done.record(comm)
     compute.wait_event(done)
-    items = []
-    for i, o in views:
-        L = ml[i]
-        p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
-        items.append((o, p, L.out.view(-1), scales[i], decays[i]))
-    run_tail(items, lr)
     return _finish_leaves(ml)

@@ -180,7 +180,7 @@ def _leaf_table(ml: list, scales, decays):
     return arr
 
 
-def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail):
+def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail, reserve_sms=0):
     cbuf, rows = coeff_buffer(ns_coeffs)
     prm = _lib.RfMuonParams()
     prm.beta = float(beta)
@@ -194,20 +194,28 @@ def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps
     prm.precision = _runtime.ns_precision()
     prm.lr = float(lr)
     prm.fuse_tail = int(fuse_tail)
+    prm.aux_stream = None
+    prm.reserve_sms = int(reserve_sms)
     return prm, cbuf
+
+
+def run_muon_table(arr, n: int, prm, dev: torch.device) -> None:
+    """rf_muon_update on a prepared leaf table, with the library's
+    preparation pipelined on the device's aux stream when enabled."""
+    lib = _lib.load()
+    pipe = _runtime.pipelined()
+    main = torch.cuda.current_stream(dev)
+    prm.aux_stream = _runtime.aux_stream(dev).cuda_stream if pipe else None
+    nbytes = ctypes.c_size_t()
+    _lib.check(lib.rf_muon_workspace_size(arr, n, prm.precision, int(pipe), ctypes.byref(nbytes)))
+    ws = _runtime.workspace(dev, nbytes.value)
+    _lib.check(lib.rf_muon_update(arr, n, ctypes.byref(prm), ws.data_ptr(), ws.numel(), main.cuda_stream))
 
 
 def _run_muon_update(ml, prm, cbuf, scales, decays):
     if not ml:
         return
-    lib = _lib.load()
-    arr = _leaf_table(ml, scales, decays)
-    nbytes = ctypes.c_size_t()
-    _lib.check(lib.rf_muon_workspace_size(arr, len(ml), prm.precision, ctypes.byref(nbytes)))
-    dev = ml[0].g.device
-    ws = _runtime.workspace(dev, nbytes.value)
-    _lib.check(lib.rf_muon_update(arr, len(ml), ctypes.byref(prm), ws.data_ptr(), ws.numel(),
-                                  stream_handle(ml[0].g)))
+    run_muon_table(_leaf_table(ml, scales, decays), len(ml), prm, ml[0].g.device)
     del cbuf
 
 
@@ -431,10 +439,11 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         for L in ml:
             on = muon_wd_on and bool(masks[L.pos]) and L.p is not None
             decays.append(round_to_dtype(float(weight_decay), L.p.dtype) if on else 0.0)
+        ctx = distributed.current()
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
-                                 ns_steps=ns_steps, lr=lr, fuse_tail=1)
-        ctx = distributed.current()
+                                 ns_steps=ns_steps, lr=lr, fuse_tail=1,
+                                 reserve_sms=ctx.reserve_sms if (ctx is not None and ctx.world_size > 1) else 0)
         if ctx is not None and ctx.world_size > 1:
             outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr)
         else:
@@ -460,8 +469,23 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             else:
                 a_items.append((g.contiguous(), amus[i], anus[i], None, out, 0.0, _lib.RF_F32))
             a_pos.append(i)
-        run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
-                 count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
+        if a_items:
+            # The fallback leaves are independent of the Muon branch: with
+            # pipelining they run on the aux stream, beside the last GEMMs.
+            dev = a_items[0][0].device
+            main = torch.cuda.current_stream(dev)
+            side = _runtime.aux_stream(dev) if _runtime.pipelined() else main
+            if side is not main:
+                side.wait_stream(main)
+            with torch.cuda.stream(side):
+                run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
+                         count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
+            if side is not main:
+                main.wait_stream(side)
+                for it in a_items:
+                    for t in it[:5]:
+                        if t is not None:
+                            t.record_stream(side)
 
         full = list(leaves)
         for L, o in zip(ml, outs):

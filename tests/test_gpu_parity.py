@@ -389,3 +389,27 @@ def test_tensor_core_kernel_variants_match_oracle(variant, shape, batch, monkeyp
     assert rel(got, ref) <= 1e-2, (variant, shape, batch, rel(got, ref))
     from rollfast_b200 import _lib
     _lib.sync_check(torch.cuda.current_stream().cuda_stream)
+
+
+def test_pipelined_and_serial_execution_are_bit_identical(monkeypatch):
+    """The aux-stream pipeline (preparation of the next shape sub-batch and
+    the AdamW leaves beside the GEMMs) changes scheduling only."""
+    import rollfast_b200 as rf
+
+    torch.manual_seed(3)
+    shapes = {"q": (512, 512), "k": (512, 128), "up": (512, 1536), "down": (1536, 512), "b": (512,),
+              "emb": (1000, 512)}
+    specs = {k: (rf.MatrixDimensionNumbers() if (len(s) == 2 and k != "emb") else None) for k, s in shapes.items()}
+    params = {k: (torch.randn(s, device=dev()) * 0.02).to(torch.bfloat16) for k, s in shapes.items()}
+    grads = [{k: torch.randn(s, device=dev()).to(torch.bfloat16) for k, s in shapes.items()} for _ in range(2)]
+    outs = {}
+    for pipe in ("0", "1"):
+        monkeypatch.setenv("ROLLFAST_PIPELINE", pipe)
+        tx = rf.muon(learning_rate=0.02, weight_decay=0.01, muon_weight_dimension_numbers=specs)
+        st = tx.init(params)
+        for g in grads:
+            u, st = tx.update(g, st, params)
+        torch.cuda.synchronize()
+        outs[pipe] = {k: v.cpu() for k, v in u.items()}
+    for k in shapes:
+        assert torch.equal(outs["0"][k], outs["1"][k]), k

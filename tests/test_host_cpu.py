@@ -55,7 +55,7 @@ def test_workspace_size_validation_without_gpu():
     leaf = _lib.RfMuonLeaf()
     leaf.batch, leaf.rows, leaf.cols = 1, 8, 8
     leaf.grad_dtype = 7
-    assert lib.rf_muon_workspace_size(ctypes.byref(leaf), 1, _lib.RF_NS_F16, ctypes.byref(n)) == _lib.RF_EINVAL
+    assert lib.rf_muon_workspace_size(ctypes.byref(leaf), 1, _lib.RF_NS_F16, 0, ctypes.byref(n)) == _lib.RF_EINVAL
     assert b"dtype" in lib.rf_last_error()
 
 
