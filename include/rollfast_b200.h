@@ -147,7 +147,10 @@ typedef struct rf_tail_leaf {
   int32_t o_dtype, param_dtype, out_dtype;
   float shape_scale, decay;
 } rf_tail_leaf;
-rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, void* stream);
+/* max_ctas_per_sm: 0 = default occupancy; 1-2 leaves room for a persistent
+ * Newton-Schulz GEMM CTA on the same SM when this runs beside it. */
+rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, int32_t max_ctas_per_sm,
+                       void* stream);
 
 /* (N)AdamW fallback leaves (adam.py:123-233 + decay + LR). */
 typedef struct rf_adam_leaf {
@@ -174,6 +177,7 @@ typedef struct rf_adam_params {
   int32_t count;      /* state.count before this step */
   int32_t nesterov;
   float lr;
+  int32_t max_ctas_per_sm;  /* as for rf_muon_tail */
 } rf_adam_params;
 rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
                           void* stream);

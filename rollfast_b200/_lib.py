@@ -118,6 +118,7 @@ class RfAdamParams(ctypes.Structure):
         ("count", ctypes.c_int32),
         ("nesterov", ctypes.c_int32),
         ("lr", ctypes.c_float),
+        ("max_ctas_per_sm", ctypes.c_int32),
     ]
 
 
@@ -164,7 +165,7 @@ def load(path: str | None = None):
                                          i32, ctypes.c_float, i32, vp, sz, vp]
         lib.rf_newton_schulz_noalloc.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float),
                                                  i32, i32, ctypes.c_float, i32, vp]
-        lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, vp]
+        lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, i32, vp]
         lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
         for name in EXPORTED:
             f = getattr(lib, name)

@@ -23,7 +23,6 @@ from .base import (
     resolve_scalar,
     round_to_dtype,
     safe_increment,
-    stream_handle,
 )
 from .tree import MaskedNode, is_aux_leaf, tree_flatten, tree_unflatten
 
@@ -61,7 +60,8 @@ def _check_mu_dtype(mu_dtype) -> None:
         )
 
 
-def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float) -> None:
+def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float,
+             max_ctas_per_sm: int = 0) -> None:
     """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype)."""
     if not items:
         return
@@ -80,8 +80,9 @@ def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: fl
         arr[i].decay = decay
         arr[i].decay_rounding = rdt
     prm = _lib.RfAdamParams(float(b1), float(b2), float(eps), float(eps_root), int(count), int(bool(nesterov)),
-                            float(lr))
-    _lib.check(lib.rf_adamw_update(arr, len(items), prm, stream_handle(items[0][0])))
+                            float(lr), int(max_ctas_per_sm))
+    _lib.check(lib.rf_adamw_update(arr, len(items), prm,
+                                   torch.cuda.current_stream(items[0][0].device).cuda_stream))
 
 
 def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_rounding_param: bool):

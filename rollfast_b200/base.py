@@ -233,7 +233,10 @@ def partition(transforms: dict, param_labels) -> GradientTransformation:
 # ---------------------------------------------------------------------------
 
 
-def run_tail(items, lr: float) -> None:
+SIDE_CTAS_PER_SM = 2  # occupancy of HBM-bound kernels run beside the persistent GEMM kernel
+
+
+def run_tail(items, lr: float, max_ctas_per_sm: int = 0) -> None:
     """items: list of (u, p_or_None, out, shape_scale, decay)."""
     if not items:
         return
@@ -249,7 +252,8 @@ def run_tail(items, lr: float) -> None:
         arr[i].out_dtype = rf_dtype(out)
         arr[i].shape_scale = scale
         arr[i].decay = decay
-    _lib.check(lib.rf_muon_tail(arr, len(items), lr, stream_handle(items[0][0])))
+    _lib.check(lib.rf_muon_tail(arr, len(items), lr, int(max_ctas_per_sm),
+                                torch.cuda.current_stream(items[0][0].device).cuda_stream))
 
 
 def _array_leaves(tree):

@@ -571,12 +571,15 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
                       static_cast<cudaStream_t>(stream), nullptr);
 }
 
-rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, void* stream) {
+rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, int32_t max_ctas_per_sm,
+                       void* stream) {
   if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  if (max_ctas_per_sm < 0) return fail(RF_EINVAL, "max_ctas_per_sm must be >= 0");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
     TailLaunch T{};
     T.neg_lr = -lr;
+    T.max_ctas_per_sm = max_ctas_per_sm;
     int64_t chunks = 0;
     for (int i = s; i < std::min(n_leaves, s + kMaxLeavesPerLaunch); ++i) {
       const rf_tail_leaf& l = leaves[i];
@@ -595,6 +598,9 @@ rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, v
       d.outdt = l.out_dtype;
       d.shape_scale = l.shape_scale;
       d.decay = l.decay;
+      d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.o) % 16 == 0) &&
+                 (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&
+                 (!l.param || reinterpret_cast<uintptr_t>(l.param) % 16 == 0);
       chunks += ceil_div(l.n, kChunk);
     }
     T.total_chunks = chunks;
@@ -609,6 +615,7 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
   if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
   const rf_adam_params& p = *params;
   if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
+  if (p.max_ctas_per_sm < 0) return fail(RF_EINVAL, "max_ctas_per_sm must be >= 0");
   AdamCoeffs c{};
   const int t = p.count + 1;
   const float b1f = float(p.b1), b2f = float(p.b2);
@@ -628,6 +635,7 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
   for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
     AdamLaunch A{};
     A.c = c;
+    A.max_ctas_per_sm = p.max_ctas_per_sm;
     int64_t chunks = 0;
     for (int i = s; i < std::min(n_leaves, s + kMaxLeavesPerLaunch); ++i) {
       const rf_adam_leaf& l = leaves[i];
@@ -649,6 +657,10 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
       d.odt = l.out_dtype;
       d.decay = l.decay;
       d.decay_dt = l.decay_rounding;
+      d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
+                 (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.nu) % 16 == 0) &&
+                 (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&
+                 (!l.param || reinterpret_cast<uintptr_t>(l.param) % 16 == 0);
       if (l.decay != 0.f && !valid_dtype(l.decay_rounding)) return fail(RF_EINVAL, "adam leaf: bad decay_rounding");
       chunks += ceil_div(l.n, kChunk);
     }

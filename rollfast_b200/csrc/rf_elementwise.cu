@@ -308,8 +308,42 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
   }
 }
 
+// 8-element vector access with a runtime (warp-uniform) dtype.
+__device__ __forceinline__ void ld8(const void* p, int dt, int64_t i, float* v) {
+  if (dt == RF_F32) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 a = q[0], b = q[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else if (dt == RF_BF16) {
+    GradVec<RF_BF16>::load8(p, i, v);
+  } else {
+    GradVec<RF_F16>::load8(p, i, v);
+  }
+}
+__device__ __forceinline__ void st8(void* p, int dt, int64_t i, const float* v) {
+  if (dt == RF_F32) store8<float>(static_cast<float*>(p) + i, v);
+  else if (dt == RF_BF16) store8<__nv_bfloat16>(static_cast<__nv_bfloat16*>(p) + i, v);
+  else store8<__half>(static_cast<__half*>(p) + i, v);
+}
+
+__device__ __forceinline__ float adam_one(const AdamCoeffs& c, const AdamLeafDev& L, float g, float& mu, float& nu,
+                                          float p) {
+  mu = __fadd_rn(__fmul_rn(c.one_minus_b1, g), __fmul_rn(c.b1, mu));
+  nu = __fadd_rn(__fmul_rn(c.one_minus_b2, __fmul_rn(g, g)), __fmul_rn(c.b2, nu));
+  float mh;
+  if (c.nesterov) {
+    mh = __fadd_rn(__fmul_rn(c.b1, __fdiv_rn(mu, c.bc1_next)), __fmul_rn(c.one_minus_b1_py, __fdiv_rn(g, c.bc1)));
+  } else {
+    mh = __fdiv_rn(mu, c.bc1);
+  }
+  const float nh = __fdiv_rn(nu, c.bc2);
+  float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(__fadd_rn(nh, c.eps_root)), c.eps));
+  if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, p));
+  return __fmul_rn(c.neg_lr, u);
+}
+
 // ---------------------------------------------------------------------------
-// k_adamw: multi-tensor (N)AdamW.
+// k_adamw: multi-tensor (N)AdamW (8-element vectors where aligned).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ AdamLaunch P) {
   __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
@@ -321,23 +355,29 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
     const AdamLeafDev& L = P.leaf[li];
     const int64_t lo = (chunk - L.chunk_begin) * kChunk;
     const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-      const float g = ld_as_float(L.g, L.gdt, i);
-      const float mu = __fadd_rn(__fmul_rn(c.one_minus_b1, g), __fmul_rn(c.b1, L.mu[i]));
-      const float nu = __fadd_rn(__fmul_rn(c.one_minus_b2, __fmul_rn(g, g)), __fmul_rn(c.b2, L.nu[i]));
-      L.mu[i] = mu;
-      L.nu[i] = nu;
-      float mh;
-      if (c.nesterov) {
-        mh = __fadd_rn(__fmul_rn(c.b1, __fdiv_rn(mu, c.bc1_next)),
-                       __fmul_rn(c.one_minus_b1_py, __fdiv_rn(g, c.bc1)));
-      } else {
-        mh = __fdiv_rn(mu, c.bc1);
+    if (L.vec_ok) {
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float g[8], mu[8], nu[8], p[8], u[8];
+        ld8(L.g, L.gdt, i, g);
+        ld8(L.mu, RF_F32, i, mu);
+        ld8(L.nu, RF_F32, i, nu);
+        if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u[k] = adam_one(c, L, g[k], mu[k], nu[k], L.decay != 0.f ? p[k] : 0.f);
+        st8(L.mu, RF_F32, i, mu);
+        st8(L.nu, RF_F32, i, nu);
+        st8(L.out, L.odt, i, u);
       }
-      const float nh = __fdiv_rn(nu, c.bc2);
-      float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(__fadd_rn(nh, c.eps_root)), c.eps));
-      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, ld_as_float(L.p, L.pdt, i)));
-      st_from_float(L.out, L.odt, i, __fmul_rn(c.neg_lr, u));
+    } else {
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float g = ld_as_float(L.g, L.gdt, i);
+        float mu = L.mu[i], nu = L.nu[i];
+        const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
+        const float u = adam_one(c, L, g, mu, nu, p);
+        L.mu[i] = mu;
+        L.nu[i] = nu;
+        st_from_float(L.out, L.odt, i, u);
+      }
     }
   }
 }
@@ -366,6 +406,12 @@ __global__ void __launch_bounds__(kEwThreads) k_direction(const __grid_constant_
 // ---------------------------------------------------------------------------
 // k_tail: out = -lr * (shape_scale * O + decay * p) for gathered leaves.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float tail_one(const TailLeafDev& L, float neg_lr, float o, float p) {
+  float u = __fmul_rn(o, L.shape_scale);
+  if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.pdt, L.decay, p));
+  return __fmul_rn(neg_lr, u);
+}
+
 __global__ void __launch_bounds__(kEwThreads) k_tail(const __grid_constant__ TailLaunch P) {
   __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
   for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
@@ -375,10 +421,20 @@ __global__ void __launch_bounds__(kEwThreads) k_tail(const __grid_constant__ Tai
     const TailLeafDev& L = P.leaf[li];
     const int64_t lo = (chunk - L.chunk_begin) * kChunk;
     const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-      float u = __fmul_rn(ld_as_float(L.o, L.odt, i), L.shape_scale);
-      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.pdt, L.decay, ld_as_float(L.p, L.pdt, i)));
-      st_from_float(L.out, L.outdt, i, __fmul_rn(P.neg_lr, u));
+    if (L.vec_ok) {
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float o[8], p[8], u[8];
+        ld8(L.o, L.odt, i, o);
+        if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u[k] = tail_one(L, P.neg_lr, o[k], L.decay != 0.f ? p[k] : 0.f);
+        st8(L.out, L.outdt, i, u);
+      }
+    } else {
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
+        st_from_float(L.out, L.outdt, i, tail_one(L, P.neg_lr, ld_as_float(L.o, L.odt, i), p));
+      }
     }
   }
 }
@@ -386,8 +442,8 @@ __global__ void __launch_bounds__(kEwThreads) k_tail(const __grid_constant__ Tai
 // ---------------------------------------------------------------------------
 // Host launchers.
 // ---------------------------------------------------------------------------
-static int ew_grid(int64_t work) {
-  const int64_t cap = int64_t(num_sms()) * 8;
+static int ew_grid(int64_t work, int ctas_per_sm = 8) {
+  const int64_t cap = int64_t(num_sms()) * (ctas_per_sm > 0 ? ctas_per_sm : 8);
   return int(work < cap ? (work > 0 ? work : 1) : cap);
 }
 
@@ -425,7 +481,7 @@ rf_status launch_ns_load(const LoadLaunch& P, int gdt, int precision, cudaStream
 
 rf_status launch_adamw(const AdamLaunch& P, cudaStream_t st) {
   if (P.total_chunks == 0) return RF_OK;
-  k_adamw<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  k_adamw<<<ew_grid(P.total_chunks, P.max_ctas_per_sm), kEwThreads, 0, st>>>(P);
   return check_launch("k_adamw");
 }
 
@@ -437,7 +493,7 @@ rf_status launch_direction(const DirLaunch& P, cudaStream_t st) {
 
 rf_status launch_tail(const TailLaunch& P, cudaStream_t st) {
   if (P.total_chunks == 0) return RF_OK;
-  k_tail<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  k_tail<<<ew_grid(P.total_chunks, P.max_ctas_per_sm), kEwThreads, 0, st>>>(P);
   return check_launch("k_tail");
 }
 

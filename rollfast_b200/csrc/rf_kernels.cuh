@@ -83,12 +83,14 @@ struct AdamLeafDev {
   void* out;
   int64_t n, chunk_begin;
   int32_t gdt, pdt, odt, decay_dt;
+  int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
   float decay;
 };
 struct AdamLaunch {
   AdamLeafDev leaf[kMaxLeavesPerLaunch];
   int n;
   int64_t total_chunks;
+  int max_ctas_per_sm;
   AdamCoeffs c;
 };
 
@@ -112,12 +114,14 @@ struct TailLeafDev {
   void* out;
   int64_t n, chunk_begin;
   int32_t odt, pdt, outdt;
+  int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
   float shape_scale, decay;
 };
 struct TailLaunch {
   TailLeafDev leaf[kMaxLeavesPerLaunch];
   int n;
   int64_t total_chunks;
+  int max_ctas_per_sm;
   float neg_lr;
 };
 

@@ -21,6 +21,7 @@ every device); ownership + all-gather is the B200 scaling design.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass, field
 from typing import Callable, Sequence
 
@@ -37,12 +38,12 @@ class ShardContext:
     world_size: int
     group: object = None
     buckets: int = 4
-    reserve_sms: int = 16
+    reserve_sms: int = 0
     plans: dict = field(default_factory=dict)
     comm_stream: object = None
 
 
-def configure(group=None, *, buckets: int = 4, reserve_sms: int = 16) -> ShardContext:
+def configure(group=None, *, buckets: int = 4, reserve_sms: int = 0) -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
 
     ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
@@ -195,7 +196,7 @@ _O_DTYPE = {_lib.RF_NS_F16: torch.float16, _lib.RF_NS_BF16: torch.bfloat16, _lib
 
 def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float):
     """Sharded version of the fused Muon-branch update (see module doc)."""
-    from .base import rf_dtype, run_tail
+    from .base import SIDE_CTAS_PER_SM, rf_dtype, run_tail
     from .muon import _finish_leaves, _leaf_table, run_muon_table
 
     if not ml:
@@ -223,9 +224,13 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     comm = ctx.comm_stream
     prm.fuse_tail = 0
 
+    trace = _Trace(compute, comm) if os.environ.get("ROLLFAST_DIST_PROFILE") == "1" else None
+
     def compute_owned(ids, offsets, send):
         # Momentum + NS for this rank's leaves of the bucket, O written (leaf
         # layout, 16-bit) straight into their segment of the send buffer.
+        if trace is not None:
+            trace.mark("compute", "ns")
         sub = [ml[i] for i in ids]
         arr = _leaf_table(sub, [1.0] * len(sub), [0.0] * len(sub))
         for j, i in enumerate(ids):
@@ -240,19 +245,51 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         # stream, beside the next bucket's GEMMs.
         ready = torch.cuda.Event()
         ready.record(compute)
+        if trace is not None:
+            trace.mark("compute", "ns_end")
         comm.wait_event(ready)
         with torch.cuda.stream(comm):
+            if trace is not None:
+                trace.mark("comm", "gather")
             exchange_bucket(send, recv, ctx.group)
+            if trace is not None:
+                trace.mark("comm", "tail")
             items = []
             for i in bucket.leaves:
                 L = ml[i]
                 o = leaf_view(bucket, recv, i, sizes[i])
                 p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
                 items.append((o, p, L.out.view(-1), scales[i], decays[i]))
-            run_tail(items, lr)
+            run_tail(items, lr, SIDE_CTAS_PER_SM)
+            if trace is not None:
+                trace.mark("comm", "tail_end")
 
     run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
     done = torch.cuda.Event()
     done.record(comm)
     compute.wait_event(done)
+    if trace is not None:
+        trace.report(ctx.rank, [sum(sizes[i] for i in b.leaves) for b in plan.buckets])
     return _finish_leaves(ml)
+
+
+class _Trace:
+    """Opt-in (ROLLFAST_DIST_PROFILE=1) timeline of the sharded update: CUDA
+    events on the compute and comm streams, printed by every rank after a
+    synchronisation (diagnostics only; it serialises the host)."""
+
+    def __init__(self, compute, comm):
+        self.streams = {"compute": compute, "comm": comm}
+        self.marks = []
+        self.t0 = torch.cuda.Event(enable_timing=True)
+        self.t0.record(compute)
+
+    def mark(self, stream: str, label: str) -> None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(self.streams[stream])
+        self.marks.append((stream, label, e))
+
+    def report(self, rank: int, bucket_elems) -> None:
+        torch.cuda.synchronize()
+        rows = [f"{st}:{lab}@{self.t0.elapsed_time(e):.2f}" for st, lab, e in self.marks]
+        print(f"[rollfast_b200 dist trace rank {rank}] buckets={list(bucket_elems)} " + " ".join(rows), flush=True)

@@ -24,6 +24,7 @@ from .adam import ScaleByAdamState, adamw, fresh_key, run_adam, zeros_like_tree
 from .base import (
     AddDecayedWeightsState,
     EmptyState,
+    SIDE_CTAS_PER_SM,
     GradientTransformation,
     MaskedState,
     PartitionState,
@@ -479,7 +480,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
                 side.wait_stream(main)
             with torch.cuda.stream(side):
                 run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
-                         count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
+                         count=host_count(adam_st.count), nesterov=nesterov, lr=alr,
+                         max_ctas_per_sm=SIDE_CTAS_PER_SM if side is not main else 0)
             if side is not main:
                 main.wait_stream(side)
                 for it in a_items:
