@@ -49,8 +49,9 @@ _aux_streams: dict = {}
 
 def pipelined() -> bool:
     """Overlap HBM-bound preparation / AdamW with the Newton-Schulz GEMMs on
-    a second stream (ROLLFAST_PIPELINE=0 turns it off)."""
-    return os.environ.get("ROLLFAST_PIPELINE", "1") != "0"
+    a second stream (ROLLFAST_PIPELINE=1; off by default: under the 1 kW power
+    cap the concurrent HBM traffic costs the GEMMs more clock than it saves)."""
+    return os.environ.get("ROLLFAST_PIPELINE", "0") != "0"
 
 
 def aux_stream(device: torch.device) -> torch.cuda.Stream:

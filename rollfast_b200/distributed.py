@@ -222,6 +222,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     if ctx.comm_stream is None:
         ctx.comm_stream = torch.cuda.Stream(device=dev)
     comm = ctx.comm_stream
+    tail_stream = _runtime.aux_stream(dev)
     prm.fuse_tail = 0
 
     trace = _Trace(compute, comm) if os.environ.get("ROLLFAST_DIST_PROFILE") == "1" else None
@@ -253,7 +254,15 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
                 trace.mark("comm", "gather")
             exchange_bucket(send, recv, ctx.group)
             if trace is not None:
-                trace.mark("comm", "tail")
+                trace.mark("comm", "gather_end")
+        # The tail gets its own stream so the next bucket's gather does not
+        # queue behind it.
+        gathered = torch.cuda.Event()
+        gathered.record(comm)
+        tail_stream.wait_event(gathered)
+        with torch.cuda.stream(tail_stream):
+            if trace is not None:
+                trace.mark("tail", "tail")
             items = []
             for i in bucket.leaves:
                 L = ml[i]
@@ -262,12 +271,13 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
                 items.append((o, p, L.out.view(-1), scales[i], decays[i]))
             run_tail(items, lr, SIDE_CTAS_PER_SM)
             if trace is not None:
-                trace.mark("comm", "tail_end")
+                trace.mark("tail", "tail_end")
 
     run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
-    done = torch.cuda.Event()
-    done.record(comm)
-    compute.wait_event(done)
+    for side in (comm, tail_stream):
+        done = torch.cuda.Event()
+        done.record(side)
+        compute.wait_event(done)
     if trace is not None:
         trace.report(ctx.rank, [sum(sizes[i] for i in b.leaves) for b in plan.buckets])
     return _finish_leaves(ml)
@@ -279,7 +289,7 @@ class _Trace:
     synchronisation (diagnostics only; it serialises the host)."""
 
     def __init__(self, compute, comm):
-        self.streams = {"compute": compute, "comm": comm}
+        self.streams = {"compute": compute, "comm": comm, "tail": _runtime.aux_stream(compute.device)}
         self.marks = []
         self.t0 = torch.cuda.Event(enable_timing=True)
         self.t0.record(compute)
