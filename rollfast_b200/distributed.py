@@ -37,18 +37,21 @@ class ShardContext:
     rank: int
     world_size: int
     group: object = None
-    buckets: int = 4
+    buckets: int = 6
     reserve_sms: int = 0
     plans: dict = field(default_factory=dict)
     comm_stream: object = None
 
 
-def configure(group=None, *, buckets: int = 4, reserve_sms: int = 0) -> ShardContext:
+def configure(group=None, *, buckets: int = 6, reserve_sms: int | None = None) -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
 
     ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
-    all-gather (NCCL) and the per-bucket tail run beside it.
+    all-gather (NCCL) runs beside it without displacing GEMM CTAs; default:
+    the NCCL channel cap ``NCCL_MAX_NCHANNELS`` when that is set, else 0.
     """
+    if reserve_sms is None:
+        reserve_sms = int(os.environ.get("NCCL_MAX_NCHANNELS", "0") or 0)
     import torch.distributed as dist
 
     global _ctx
@@ -106,15 +109,23 @@ class ShardPlan:
     loads: list[int]
 
 
+def bucket_weights(n_buckets: int) -> list[float]:
+    """Cost shares of the buckets: small first (the first gather starts
+    early), large in the middle, small last (the exposed final gather and
+    tail are short).  E.g. 6 -> [1, 2, 4, 4, 2, 1]."""
+    if n_buckets <= 2:
+        return [2.0, 1.0][:n_buckets] if n_buckets == 2 else [1.0]
+    half = [2.0 ** k for k in range((n_buckets + 1) // 2)]
+    return half + half[::-1][n_buckets % 2:]
+
+
 def make_plan(sizes: Sequence[int], costs: Sequence[int], world_size: int, n_buckets: int) -> ShardPlan:
-    """Ownership + bucket layout.  Buckets split the leaf list (in order) into
-    ``n_buckets`` runs of roughly equal total cost, the last one smallest so
-    the exposed final all-gather is short."""
+    """Ownership + bucket layout: the leaf list (in order) is cut into
+    ``n_buckets`` runs whose NS costs follow ``bucket_weights``."""
     owner = lpt_assign(costs, world_size)
     n = len(sizes)
     total = sum(costs) or 1
-    # Cost targets decreasing geometrically towards the end.
-    weights = [2.0 ** (n_buckets - 1 - k) for k in range(n_buckets)]
+    weights = bucket_weights(n_buckets)
     wsum = sum(weights)
     bounds, acc, k = [], 0.0, 0
     target = weights[0] / wsum * total
