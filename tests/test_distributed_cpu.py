@@ -66,8 +66,7 @@ def test_bucket_weights_shape():
     from rollfast_b200.distributed import bucket_weights
 
     assert bucket_weights(1) == [1.0]
-    assert bucket_weights(6) == [1.0, 2.0, 4.0, 4.0, 2.0, 1.0]
-    assert bucket_weights(5) == [1.0, 2.0, 4.0, 2.0, 1.0]
+    assert bucket_weights(4) == [8.0, 4.0, 2.0, 1.0]
 
 
 def _free_port():
