@@ -44,12 +44,12 @@ FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_g
 # Workload
 # ---------------------------------------------------------------------------
 
-def llama3_8b_shapes():
+def llama3_8b_shapes(layers: int = 32, vocab: int = 128256):
     layer = {"q": (4096, 4096), "k": (4096, 1024), "v": (4096, 1024), "o": (4096, 4096),
              "gate": (4096, 14336), "up": (4096, 14336), "down": (14336, 4096),
              "attn_norm": (4096,), "mlp_norm": (4096,)}
-    return {"layers": [dict(layer) for _ in range(32)], "final_norm": (4096,),
-            "embed": (128256, 4096), "unembed": (128256, 4096)}
+    return {"layers": [dict(layer) for _ in range(layers)], "final_norm": (4096,),
+            "embed": (vocab, 4096), "unembed": (vocab, 4096)}
 
 
 def muon_specs(shapes, rf):
@@ -269,6 +269,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=32,
+                    help="reduced-size case for kernel profiles only (the headline is 32 layers)")
+    ap.add_argument("--vocab", type=int, default=128256)
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -294,7 +297,7 @@ def main():
         rf.distributed.configure()
     rf.set_ns_precision(args.precision)
 
-    shapes = llama3_8b_shapes()
+    shapes = llama3_8b_shapes(args.layers, args.vocab)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)
 
@@ -377,8 +380,11 @@ def main():
             "vs_baseline": None,
             "dtype": f"{args.precision} NS operands, fp32 accumulate/state, bf16 params+grads",
             "data": "synthetic: N(0,1) bf16 grads (2 seeded sets), N(0,0.02) bf16 params",
-            "config": {"workload": "llama3_8b_muon_step", "model": "Llama-3-8B (32 layers) parameter set",
-                       "muon_leaves": 224, "adam_leaves": 67, "ns_steps": 5, "ns_coeffs": "standard",
+            "config": {"workload": "llama3_8b_muon_step" if (args.layers, args.vocab) == (32, 128256)
+                       else f"reduced_{args.layers}_layers_vocab_{args.vocab}",
+                       "model": f"Llama-3-8B ({args.layers} layers) parameter set",
+                       "muon_leaves": 7 * args.layers, "adam_leaves": 2 * args.layers + 3, "ns_steps": 5,
+                       "ns_coeffs": "standard",
                        "l2": "inputs (16 GB grads) >> 126 MB L2; no flush",
                        "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)"
                        + (", NCCL all-gather" if world > 1 else "")},
