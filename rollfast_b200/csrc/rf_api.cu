@@ -77,6 +77,8 @@ static MomentumCoeffs momentum_coeffs(const rf_muon_params& p) {
     c.bc_mu = c.bc_g = 1.0f;                                            // utils.py:503-504
     c.mode = p.nesterov ? kDirHeavyBallNesterov : kDirHeavyBall;
   }
+  c.rbc_mu = float(1.0 / double(c.bc_mu));
+  c.rbc_g = float(1.0 / double(c.bc_g));
   return c;
 }
 

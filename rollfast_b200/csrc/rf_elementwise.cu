@@ -40,6 +40,25 @@ __device__ __forceinline__ float direction(const MomentumCoeffs& c, float g, flo
   }
 }
 
+// The same direction with reciprocal multiplies instead of IEEE divisions:
+// used only where the result is immediately rounded to the 16-bit (or
+// scaled float32) Newton-Schulz operand, so the last-bit difference never
+// reaches the momentum state.
+__device__ __forceinline__ float direction_fast(const MomentumCoeffs& c, float g, float mu_new) {
+  switch (c.mode) {
+    case kDirEmaNesterov:
+      return fmaf(c.beta * c.rbc_mu, mu_new, c.s * c.rbc_g * g);
+    case kDirEma:
+      return mu_new * c.rbc_mu;
+    case kDirHeavyBallNesterov:
+      return fmaf(c.beta, mu_new, c.s * g);
+    case kDirHeavyBall:
+      return mu_new;
+    default:
+      return g;
+  }
+}
+
 template <int GDT>
 struct GradVec;
 template <>
@@ -184,7 +203,7 @@ __global__ void __launch_bounds__(kEwThreads) k_norm_finalize(const __grid_const
 }
 
 // ---------------------------------------------------------------------------
-// k_ns_load: builds the padded NS operand X~0 = round(sx * (d / (||d|| + eps)))
+// k_ns_load: builds the padded NS operand X~0 = round(d * (sx / (||d|| + eps)))
 // for every matrix of one shape group, 64x64 output tiles.  Each thread
 // moves 8-element vectors (16-byte grad / operand accesses, 32-byte mu).
 // A leaf with rows <= cols maps straight onto the operand; a transposed leaf
@@ -224,7 +243,7 @@ __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const fl
 // outside the leaf).
 template <int GDT>
 __device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int64_t base, int64_t ir, int64_t ic,
-                                     float denom, float* v) {
+                                     float scale, float* v) {
   if (ir < L.rows && ic + 7 < L.cols && L.vec_ok) {
     const int64_t idx = base + ir * L.cols + ic;
     float g[8], m[8];
@@ -238,7 +257,7 @@ __device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int
       for (int k = 0; k < 8; ++k) m[k] = 0.f;
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fdiv_rn(direction(P.c, g[k], m[k]), denom), P.sx);
+    for (int k = 0; k < 8; ++k) v[k] = direction_fast(P.c, g[k], m[k]) * scale;
   } else {
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -248,7 +267,7 @@ __device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int
         const int64_t idx = base + ir * L.cols + c;
         const float g = ld_as_float(L.g, GDT, idx);
         const float m = L.mu ? L.mu[idx] : 0.f;
-        x = __fmul_rn(__fdiv_rn(direction(P.c, g, m), denom), P.sx);
+        x = direction_fast(P.c, g, m) * scale;
       }
       v[k] = x;
     }
@@ -274,14 +293,15 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
     if (L.gdt != GDT) continue;  // uniform per tile: another launch covers it
     const int64_t bi = gm - L.group_mat_begin;
     const int64_t base = bi * L.rows * L.cols;
-    const float denom = P.denom[L.norm_index + bi];
+    // sx / (||d|| + eps): one division per tile; sx is a power of two.
+    const float scale = P.sx / P.denom[L.norm_index + bi];
     OT* out = static_cast<OT*>(P.x) + gm * P.mp * P.np;
     if (!L.transposed) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int64_t r = r0 + tr + 32 * h;
         float v[8];
-        dir8<GDT>(P, L, base, r, c0 + tc, denom, v);
+        dir8<GDT>(P, L, base, r, c0 + tc, scale, v);
         store8<OT>(out + r * P.np + c0 + tc, v);
       }
     } else {
@@ -291,7 +311,7 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
       for (int h = 0; h < 2; ++h) {
         const int lr = tr + 32 * h;
         float v[8];
-        dir8<GDT>(P, L, base, c0 + lr, r0 + tc, denom, v);
+        dir8<GDT>(P, L, base, c0 + lr, r0 + tc, scale, v);
 #pragma unroll
         for (int k = 0; k < 8; ++k) tile[lr][tc + k] = v[k];
       }

@@ -25,6 +25,7 @@ struct MomentumCoeffs {
   float beta;
   float bc_mu;  // 1 - beta^(t+1) under Nesterov, else 1 - beta^t (ema only)
   float bc_g;   // 1 - beta^t (ema + Nesterov only)
+  float rbc_mu, rbc_g;  // reciprocals, for the operand load (rounded to 16 bits afterwards)
   int mode;     // DirMode
 };
 
