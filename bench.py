@@ -38,6 +38,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Llama-3-8B Muon step ms at 1/2/4/8 B200; NS bf16 TFLOP/s vs peak"
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+# ncu: 2-matrix capture, 15 stage launches of a 5-iteration NS = 6738 MB -> 449 MB per launch; x 48/2.
+TRAFFIC_PER_LAUNCH = round(6738e6 / 15 * 24)
 
 
 # ---------------------------------------------------------------------------
@@ -400,7 +402,13 @@ def main():
                 "executed_tflops": round(executed, 1) if executed else None,
                 "launches": prof["launches"],
                 "gemm_ms_per_step": round(prof["gemm_ms"] / args.steps, 2),
-                "traffic": None,
+                # DRAM read+write bytes per launch of the 4096x14336 sub-batch
+                # stages (80% of the step's FLOPs), from the ncu capture in
+                # profiles/k_ns_tc2_4096x14336_b2.md: 449 MB per launch at 2
+                # matrices, scaled to the bench's 48-matrix launches (the
+                # per-matrix working set exceeds L2, so bytes grow with it).
+                "traffic": TRAFFIC_PER_LAUNCH if (args.layers, args.vocab) == (32, 128256) else None,
+                "traffic_unit": "bytes per launch",
             },
             "gpu_launches": launches,
             "clocks": clocks.summary(),
