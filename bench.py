@@ -109,18 +109,28 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval_ms: int = 50):
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
         self.lines = []
+        self.skip = 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                 str(self.interval_ms), "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait for its first sample
+            # (taken before the timed region, so it is not counted) so that
+            # even a sub-second timed region is sampled.
+            t0 = time.monotonic()
+            while not self.lines and self.proc.poll() is None and time.monotonic() - t0 < 10.0:
+                time.sleep(0.01)
+            self.skip = len(self.lines)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -140,7 +150,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.skip:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
                 continue
@@ -389,7 +399,9 @@ def main():
                        "ns_coeffs": "standard",
                        "l2": "inputs (16 GB grads) >> 126 MB L2; no flush",
                        "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)"
-                       + (", NCCL all-gather" if world > 1 else "")},
+                       + ({"ce": ", copy-engine all-gather into IPC-mapped peer buffers",
+                           "nccl": ", NCCL all-gather"}.get(rf.distributed.active_transport(), "")
+                          if world > 1 else "")},
             "ns_tflops_algorithmic": round(ns_alg_flops(shapes) / (ms * 1e-3) / 1e12, 1),
             "roofline": {
                 "bound": "tensor",
@@ -417,6 +429,7 @@ def main():
         }
         print(json.dumps(out), flush=True)
     if dist is not None:
+        rf.distributed.clear()  # collective: unmaps the peers' buffers once every rank is idle
         dist.barrier()
         dist.destroy_process_group()
 

@@ -182,6 +182,41 @@ typedef struct rf_adam_params {
 rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
                           void* stream);
 
+/* ------------------------------------------------------------------------
+ * Peer transport for the multi-GPU Muon update (one process per GPU, one
+ * node).  No reference counterpart: the reference runs every Muon leaf on
+ * every device.  The sharded update gathers each owner's orthogonalised
+ * leaves by pushing them with the copy engines into the other ranks' buffers
+ * (mapped through CUDA IPC), so the gather takes no SMs from the
+ * Newton-Schulz GEMMs; cross-rank ordering uses 32-bit epoch flags.
+ * ------------------------------------------------------------------------ */
+typedef struct rf_ipc_handle {
+  unsigned char bytes[64];  /* a cudaIpcMemHandle_t */
+} rf_ipc_handle;
+
+/* Handle of the device allocation that contains `ptr` (memory from
+ * cudaMalloc, e.g. the PyTorch caching allocator's segments), and the byte
+ * offset of `ptr` from the allocation's base. */
+rf_status rf_ipc_export(const void* ptr, rf_ipc_handle* handle, size_t* offset);
+/* Maps another process's allocation into the current device's context (peer
+ * access enabled on demand) and returns its base; the same handle opened
+ * twice returns the same base.  Add the exporter's offset. */
+rf_status rf_ipc_open(const rf_ipc_handle* handle, void** base);
+/* Releases one rf_ipc_open of `base`; the mapping goes with the last. */
+rf_status rf_ipc_close(void* base);
+/* Stream-ordered copy engine copy of `bytes` between device pointers of
+ * this or a mapped peer allocation (no kernel). */
+rf_status rf_peer_copy(void* dst, const void* src, size_t bytes, void* stream);
+/* After the stream's prior work: a system-scope release store of `value` to
+ * each flags[i] (local or mapped peer addresses; n <= 64). */
+rf_status rf_flags_signal(uint32_t* const* flags, int32_t n, uint32_t value, void* stream);
+/* Blocks the stream until every flags[i] (i != skip, n <= 64, local memory)
+ * reaches `target` (wrap-around compare), polling with system-scope acquire
+ * loads for at most `timeout_s`; on expiry the wait gives up, the stream moves
+ * on and the next rf_sync_check reports RF_ETIMEOUT. */
+rf_status rf_flags_wait(const uint32_t* flags, int32_t n, int32_t skip, uint32_t target, double timeout_s,
+                        void* stream);
+
 /* Diagnostics. */
 const char* rf_last_error(void);
 rf_status rf_version(int32_t* major, int32_t* minor, int32_t* patch);

@@ -40,7 +40,17 @@ EXPORTED = (
     "rf_sync_check",
     "rf_profile_begin",
     "rf_profile_end",
+    "rf_ipc_export",
+    "rf_ipc_open",
+    "rf_ipc_close",
+    "rf_peer_copy",
+    "rf_flags_signal",
+    "rf_flags_wait",
 )
+
+
+class RfIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 class RfMuonLeaf(ctypes.Structure):
@@ -167,6 +177,12 @@ def load(path: str | None = None):
                                                  i32, i32, ctypes.c_float, i32, vp]
         lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, i32, vp]
         lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
+        lib.rf_ipc_export.argtypes = [vp, ctypes.POINTER(RfIpcHandle), ctypes.POINTER(sz)]
+        lib.rf_ipc_open.argtypes = [ctypes.POINTER(RfIpcHandle), ctypes.POINTER(vp)]
+        lib.rf_ipc_close.argtypes = [vp]
+        lib.rf_peer_copy.argtypes = [vp, vp, sz, vp]
+        lib.rf_flags_signal.argtypes = [ctypes.POINTER(vp), i32, ctypes.c_uint32, vp]
+        lib.rf_flags_wait.argtypes = [vp, i32, i32, ctypes.c_uint32, ctypes.c_double, vp]
         for name in EXPORTED:
             f = getattr(lib, name)
             if name not in ("rf_last_error", "rf_kernel_launch_count"):
@@ -206,3 +222,46 @@ def profile_end() -> dict:
     alg, exe = ctypes.c_double(), ctypes.c_double()
     check(load().rf_profile_end(ctypes.byref(ms), ctypes.byref(n), ctypes.byref(alg), ctypes.byref(exe)))
     return {"gemm_ms": ms.value, "launches": n.value, "algorithmic_flops": alg.value, "executed_flops": exe.value}
+
+
+# ---------------------------------------------------------------------------
+# Peer transport (multi-GPU sharded update)
+# ---------------------------------------------------------------------------
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(64-byte IPC handle of the allocation holding ``ptr``, offset of ``ptr`` in it)."""
+    h, off = RfIpcHandle(), ctypes.c_size_t()
+    check(load().rf_ipc_export(ctypes.c_void_p(ptr), ctypes.byref(h), ctypes.byref(off)))
+    return bytes(h.bytes), int(off.value)
+
+
+def ipc_open(handle: bytes) -> int:
+    """Base address of another process's allocation mapped into the current device."""
+    if len(handle) != 64:
+        raise ValueError("an IPC handle is 64 bytes")
+    h = RfIpcHandle()
+    ctypes.memmove(h.bytes, handle, 64)
+    base = ctypes.c_void_p()
+    check(load().rf_ipc_open(ctypes.byref(h), ctypes.byref(base)))
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    check(load().rf_ipc_close(ctypes.c_void_p(base)))
+
+
+def peer_copy(dst: int, src: int, nbytes: int, stream_handle: int) -> None:
+    check(load().rf_peer_copy(ctypes.c_void_p(dst), ctypes.c_void_p(src), ctypes.c_size_t(nbytes),
+                              ctypes.c_void_p(stream_handle)))
+
+
+def flags_signal(addrs, value: int, stream_handle: int) -> None:
+    arr = (ctypes.c_void_p * max(len(addrs), 1))(*addrs)
+    check(load().rf_flags_signal(arr, len(addrs), ctypes.c_uint32(value & 0xFFFFFFFF),
+                                 ctypes.c_void_p(stream_handle)))
+
+
+def flags_wait(addr: int, n: int, skip: int, target: int, timeout_s: float, stream_handle: int) -> None:
+    check(load().rf_flags_wait(ctypes.c_void_p(addr), n, skip, ctypes.c_uint32(target & 0xFFFFFFFF),
+                               float(timeout_s), ctypes.c_void_p(stream_handle)))

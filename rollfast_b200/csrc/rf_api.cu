@@ -55,6 +55,7 @@ int num_sms() {
 }
 
 rf_status take_device_error();  // rf_ns_tc.cu
+rf_status take_peer_error();    // rf_peer.cu
 
 // ---------------------------------------------------------------------------
 // Host-side scalar factors, formed in float32 like the reference.
@@ -453,6 +454,7 @@ int64_t rf_kernel_launch_count(void) { return g_launches.load(); }
 rf_status rf_sync_check(void* stream) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(RF_ECUDA, std::string("stream sync: ") + cudaGetErrorString(e));
+  RF_TRY(take_peer_error());
   return take_device_error();
 }
 

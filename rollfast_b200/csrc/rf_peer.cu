@@ -1,0 +1,227 @@
+// Peer transport for the sharded multi-GPU Muon update: CUDA IPC mappings of
+// other ranks' buffers, copy engine pushes into them, and 32-bit epoch flags
+// that order the ranks' work without a host round trip.
+//
+// Why the copy engines: on 8 B200s a copy engine push of 11 GB per rank runs
+// at ~700 GB/s and slows a concurrent tcgen05 GEMM by ~3%, while an NCCL
+// all-gather of the same bytes needs SMs and stretches the GEMM by 15-35%.
+//
+// Ordering protocol (driven by rollfast_b200/distributed.py):
+//   * owner:    GEMM writes O into its slot -> copy engine pushes the slot into
+//               every peer's buffer -> rf_flags_signal(arrive[k] on peers)
+//   * receiver: rf_flags_wait(arrive[k] >= epoch) -> tail kernel reads the
+//               gathered bucket from local memory
+//   * at the end of a step each rank signals ack = epoch to its peers; an
+//     owner waits for ack >= epoch - 1 from all peers before its first push
+//     of a step, so a slot is never overwritten while its reader still reads.
+// A copy engine copy is complete (its writes visible to the destination
+// device) before the next operation on its stream starts, so a flag stored
+// by the following kernel is observed only after the data.
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "rf_common.cuh"
+
+namespace rf {
+namespace peer {
+
+constexpr int kMaxFlags = 64;
+
+__device__ int g_peer_error = 0;  // 1 once a flag wait gave up
+
+struct SignalArgs {
+  uint32_t* flags[kMaxFlags];
+  int32_t n;
+  uint32_t value;
+};
+
+struct WaitArgs {
+  const uint32_t* flags;
+  int32_t n;
+  int32_t skip;
+  uint32_t target;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void k_flags_signal(SignalArgs a) {
+  const int i = threadIdx.x;
+  if (i < a.n) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[i]), "r"(a.value) : "memory");
+  }
+}
+
+__global__ void k_flags_wait(WaitArgs a) {
+  const int i = threadIdx.x;
+  if (i < a.n && i != a.skip) {
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.flags + i) : "memory");
+      if (static_cast<int32_t>(v - a.target) >= 0) break;
+      if (globaltimer() - t0 > a.timeout_ns) {
+        atomicExch(&g_peer_error, 1);
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// IPC bookkeeping: one mapping per (device, allocation handle), reference
+// counted, because a context may map an allocation only once.
+// ---------------------------------------------------------------------------
+struct Mapping {
+  void* base;
+  int refs;
+  int device;
+};
+
+std::mutex g_mu;
+std::map<std::pair<int, std::string>, Mapping> g_by_handle;
+std::map<void*, std::pair<int, std::string>> g_by_base;
+
+using PFN_getAddressRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+PFN_getAddressRange address_range_fn() {
+  static PFN_getAddressRange fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_getAddressRange>(p);
+  });
+  return fn;
+}
+
+rf_status cuda_fail(const char* what, cudaError_t e) {
+  return fail(RF_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace peer
+
+// Reads and clears the flag-wait error word.
+rf_status take_peer_error() {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, peer::g_peer_error, sizeof(int));
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string("reading peer error word: ") + cudaGetErrorString(e));
+  if (v != 0) {
+    int zero = 0;
+    cudaMemcpyToSymbol(peer::g_peer_error, &zero, sizeof(int));
+    return fail(RF_ETIMEOUT, "a cross-rank flag wait gave up (a peer did not reach the step)");
+  }
+  return RF_OK;
+}
+
+}  // namespace rf
+
+using namespace rf;
+
+extern "C" {
+
+rf_status rf_ipc_export(const void* ptr, rf_ipc_handle* handle, size_t* offset) {
+  if (!ptr || !handle || !offset) return fail(RF_EINVAL, "rf_ipc_export: null pointer");
+  auto fn = peer::address_range_fn();
+  if (!fn) return fail(RF_ECUDA, "cuMemGetAddressRange entry point unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(RF_EINVAL, "rf_ipc_export: pointer is not in a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return peer::cuda_fail("cudaIpcGetMemHandle", e);
+  static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+  memcpy(handle->bytes, &h, sizeof(h));
+  *offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return RF_OK;
+}
+
+rf_status rf_ipc_open(const rf_ipc_handle* handle, void** base) {
+  if (!handle || !base) return fail(RF_EINVAL, "rf_ipc_open: null pointer");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return peer::cuda_fail("cudaGetDevice", e);
+  const std::pair<int, std::string> key(dev, std::string(reinterpret_cast<const char*>(handle->bytes), 64));
+  std::lock_guard<std::mutex> lk(peer::g_mu);
+  auto it = peer::g_by_handle.find(key);
+  if (it != peer::g_by_handle.end()) {
+    it->second.refs++;
+    *base = it->second.base;
+    return RF_OK;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  void* p = nullptr;
+  e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return peer::cuda_fail("cudaIpcOpenMemHandle", e);
+  peer::g_by_handle[key] = peer::Mapping{p, 1, dev};
+  peer::g_by_base[p] = key;
+  *base = p;
+  return RF_OK;
+}
+
+rf_status rf_ipc_close(void* base) {
+  std::lock_guard<std::mutex> lk(peer::g_mu);
+  auto it = peer::g_by_base.find(base);
+  if (it == peer::g_by_base.end()) return fail(RF_EINVAL, "rf_ipc_close: not a mapping made by rf_ipc_open");
+  auto m = peer::g_by_handle.find(it->second);
+  if (--m->second.refs > 0) return RF_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != m->second.device) cudaSetDevice(m->second.device);
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (cur != m->second.device) cudaSetDevice(cur);
+  peer::g_by_handle.erase(m);
+  peer::g_by_base.erase(it);
+  if (e != cudaSuccess) return peer::cuda_fail("cudaIpcCloseMemHandle", e);
+  return RF_OK;
+}
+
+rf_status rf_peer_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return RF_OK;
+  if (!dst || !src) return fail(RF_EINVAL, "rf_peer_copy: null pointer");
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return peer::cuda_fail("cudaMemcpyAsync (peer push)", e);
+  return RF_OK;
+}
+
+rf_status rf_flags_signal(uint32_t* const* flags, int32_t n, uint32_t value, void* stream) {
+  if (n < 0 || n > peer::kMaxFlags) return fail(RF_EINVAL, "rf_flags_signal: n must be in [0, 64]");
+  if (n == 0) return RF_OK;
+  if (!flags) return fail(RF_EINVAL, "rf_flags_signal: null flags");
+  peer::SignalArgs a{};
+  for (int i = 0; i < n; ++i) {
+    if (!flags[i] || (reinterpret_cast<uintptr_t>(flags[i]) & 3))
+      return fail(RF_EINVAL, "rf_flags_signal: flag pointers must be non-null and 4-byte aligned");
+    a.flags[i] = flags[i];
+  }
+  a.n = n;
+  a.value = value;
+  peer::k_flags_signal<<<1, peer::kMaxFlags, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("k_flags_signal");
+}
+
+rf_status rf_flags_wait(const uint32_t* flags, int32_t n, int32_t skip, uint32_t target, double timeout_s,
+                        void* stream) {
+  if (n < 0 || n > peer::kMaxFlags) return fail(RF_EINVAL, "rf_flags_wait: n must be in [0, 64]");
+  if (n == 0) return RF_OK;
+  if (!flags || (reinterpret_cast<uintptr_t>(flags) & 3))
+    return fail(RF_EINVAL, "rf_flags_wait: flags must be non-null and 4-byte aligned");
+  if (!(timeout_s > 0.0) || timeout_s > 600.0) return fail(RF_EINVAL, "rf_flags_wait: timeout_s must be in (0, 600]");
+  peer::WaitArgs a{flags, n, skip, target, static_cast<uint64_t>(timeout_s * 1e9)};
+  peer::k_flags_wait<<<1, peer::kMaxFlags, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("k_flags_wait");
+}
+
+}  // extern "C"

@@ -6,10 +6,15 @@ gradients of all leaves.  The Muon leaves are assigned to ranks by
 longest-processing-time-first on their Newton-Schulz FLOPs
 (4 m^2 n + 2 m^3 per matrix per iteration, m <= n); each rank runs the
 momentum + Newton-Schulz pipeline for its own leaves only, writing O in the
-leaf layout into its segment of a packed buffer, and an NCCL all-gather over
-NVLink returns every rank's segments.  Buckets of leaves are gathered on a
-side stream while the next bucket's Newton-Schulz runs.  Every rank then
-applies the tail -lr (shape * O + decay * p) to all leaves.
+leaf layout into its slot of a per-bucket gathered buffer, and the slots are
+exchanged bucket by bucket while the next bucket's Newton-Schulz runs:
+
+* ``transport="ce"`` (default when every rank is on one host): the copy
+  engines push each owner's slot into the peers' IPC-mapped buffers, ordered
+  by device-side epoch flags (``peer.py``); the gather uses no SMs;
+* ``transport="nccl"``: ``all_gather_into_tensor`` on a side stream.
+
+Every rank then applies the tail -lr (shape * O + decay * p) to all leaves.
 
 Momentum for a leaf is kept current only on the rank that owns it; the
 ownership plan is deterministic for a given leaf list and world size.
@@ -41,10 +46,28 @@ class ShardContext:
     reserve_sms: int = 0
     plans: dict = field(default_factory=dict)
     comm_stream: object = None
+    transport: str = "nccl"           # "ce" | "nccl" | "auto" (ce, else nccl)
+
+    def close(self) -> None:
+        """Releases the plans' peer mappings (collective when any exist)."""
+        for entry in self.plans.values():
+            gather = entry[2]
+            if gather is not None:
+                gather.close()
+        self.plans.clear()
 
 
-def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None = None) -> ShardContext:
+TRANSPORTS = ("auto", "ce", "nccl")
+
+
+def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None = None,
+              transport: str | None = None) -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
+
+    ``transport``: how owners' leaves reach the other ranks: ``"ce"`` (copy
+    engine pushes into IPC-mapped peer buffers; one host only), ``"nccl"``
+    (all-gather), or ``"auto"`` (default; ``ROLLFAST_DIST_GATHER`` overrides):
+    ``ce`` when every rank can map its peers' memory, else ``nccl``.
 
     ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
     all-gather (NCCL) runs beside it without displacing GEMM CTAs; default:
@@ -54,13 +77,20 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
         reserve_sms = int(os.environ.get("NCCL_MAX_NCHANNELS", "0") or 0)
     if buckets is None:
         buckets = int(os.environ.get("ROLLFAST_DIST_BUCKETS", "4") or 4)
+    if transport is None:
+        transport = os.environ.get("ROLLFAST_DIST_GATHER", "auto") or "auto"
+    transport = transport.lower()
+    if transport not in TRANSPORTS:
+        raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
     import torch.distributed as dist
 
     global _ctx
     if not dist.is_initialized():
         raise RuntimeError("torch.distributed must be initialised before rollfast_b200.distributed.configure")
+    if _ctx is not None:
+        _ctx.close()
     _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
-                        buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)))
+                        buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)), transport=transport)
     return _ctx
 
 
@@ -68,8 +98,20 @@ def current() -> ShardContext | None:
     return _ctx
 
 
-def clear() -> None:
+def use(ctx: ShardContext | None) -> ShardContext | None:
+    """Make ``ctx`` (or no sharding, for None) current without releasing the
+    previous context's resources; returns the previous context."""
     global _ctx
+    prev, _ctx = _ctx, ctx
+    return prev
+
+
+def clear() -> None:
+    """Turn sharding off.  Collective when the copy-engine transport has
+    mapped peer buffers: every rank of the group must call it."""
+    global _ctx
+    if _ctx is not None:
+        _ctx.close()
     _ctx = None
 
 
@@ -97,11 +139,16 @@ def lpt_assign(costs: Sequence[int], world_size: int) -> list[int]:
     return owner
 
 
+SEG_ALIGN = 64  # elements: segments start 128-byte aligned for 16-bit O (vectorised tail loads)
+
+
 @dataclass
 class BucketPlan:
     leaves: list[int]                 # global leaf indices in this bucket
-    seg: int                          # per-rank segment length (elements)
+    seg: int                          # per-rank segment length (elements, multiple of SEG_ALIGN)
     offsets: dict                     # leaf -> (owner, offset within owner's segment)
+    used: list = field(default_factory=list)  # elements of each rank's segment holding leaves
+    index: int = 0                    # position in ShardPlan.buckets
 
 
 @dataclass
@@ -148,7 +195,8 @@ def make_plan(sizes: Sequence[int], costs: Sequence[int], world_size: int, n_buc
             r = owner[i]
             offsets[i] = (r, used[r])
             used[r] += sizes[i]
-        buckets.append(BucketPlan(list(range(lo, hi)), max(used) if used else 0, offsets))
+        seg = (max(used) + SEG_ALIGN - 1) // SEG_ALIGN * SEG_ALIGN if used else 0
+        buckets.append(BucketPlan(list(range(lo, hi)), seg, offsets, used, len(buckets)))
     loads = [0] * world_size
     for i, r in enumerate(owner):
         loads[r] += costs[i]
@@ -209,6 +257,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     """Sharded version of the fused Muon-branch update (see module doc)."""
     from .base import SIDE_CTAS_PER_SM, rf_dtype, run_tail
     from .muon import _finish_leaves, _leaf_table, run_muon_table
+    from .peer import PeerGather
 
     if not ml:
         return []
@@ -221,22 +270,29 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         steps = prm.n_coeff_rows or prm.ns_steps
         costs = [ns_flops(*L.layout.flat_shape) * steps for L in ml]
         plan = make_plan(sizes, costs, ctx.world_size, ctx.buckets)
-        # Stream order makes reuse safe: a bucket's send buffer is rewritten
-        # only after the compute stream waited for the previous step's
-        # gathers, and its recv buffer is regathered only after this step's
-        # tail (compute stream) has read it.
-        entry = (plan, bucket_buffers(plan, ctx.world_size, odt, dev))
+        gather = None
+        if ctx.transport in ("ce", "auto") and ctx.world_size > 1:
+            gather = PeerGather.create(plan, ctx, odt, dev, required=ctx.transport == "ce")
+        # Stream order makes reuse of the NCCL buffers safe: a bucket's send
+        # buffer is rewritten only after the compute stream waited for the
+        # previous step's gathers, and its recv buffer is regathered only
+        # after the tail has read it.  The copy-engine buffers are guarded by
+        # the epoch flags (peer.py).
+        buffers = gather.buffers if gather is not None else bucket_buffers(plan, ctx.world_size, odt, dev)
+        entry = (plan, buffers, gather)
         ctx.plans[key] = entry
-    plan, buffers = entry
-    lib = _lib.load()
+    plan, buffers, gather = entry
     compute = torch.cuda.current_stream(dev)
-    if ctx.comm_stream is None:
+    # Streams per rank: compute, tail, and either one copy stream (peer.py)
+    # or the NCCL side stream, well inside the device's hardware queues.
+    if gather is None and ctx.comm_stream is None:
         ctx.comm_stream = torch.cuda.Stream(device=dev)
     comm = ctx.comm_stream
     tail_stream = _runtime.aux_stream(dev)
     prm.fuse_tail = 0
 
-    trace = _Trace(compute, comm) if os.environ.get("ROLLFAST_DIST_PROFILE") == "1" else None
+    side = gather.copy_stream if gather is not None else comm
+    trace = _Trace(compute, side) if os.environ.get("ROLLFAST_DIST_PROFILE") == "1" else None
 
     def compute_owned(ids, offsets, send):
         # Momentum + NS for this rank's leaves of the bucket, O written (leaf
@@ -250,11 +306,25 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
             arr[j].out_dtype = rf_dtype(send)
         run_muon_table(arr, len(sub), prm, dev)
 
-    def exchange(bucket, send, recv):
+    def tail(bucket, recv):
+        # -lr (shape O + decay p) for all the bucket's leaves, on the tail
+        # stream beside the next bucket's GEMMs.
+        with torch.cuda.stream(tail_stream):
+            if trace is not None:
+                trace.mark("tail", "tail")
+            items = []
+            for i in bucket.leaves:
+                L = ml[i]
+                o = leaf_view(bucket, recv, i, sizes[i])
+                p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+                items.append((o, p, L.out.view(-1), scales[i], decays[i]))
+            run_tail(items, lr, SIDE_CTAS_PER_SM)
+            if trace is not None:
+                trace.mark("tail", "tail_end")
+
+    def exchange_nccl(bucket, send, recv):
         # Gather on the side stream once this bucket's NS is done, while the
-        # compute stream moves on to the next bucket; the bucket's tail
-        # (-lr (shape O + decay p) for all its leaves) follows on the same
-        # stream, beside the next bucket's GEMMs.
+        # compute stream moves on to the next bucket.
         ready = torch.cuda.Event()
         ready.record(compute)
         if trace is not None:
@@ -271,27 +341,60 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         gathered = torch.cuda.Event()
         gathered.record(comm)
         tail_stream.wait_event(gathered)
-        with torch.cuda.stream(tail_stream):
-            if trace is not None:
-                trace.mark("tail", "tail")
-            items = []
-            for i in bucket.leaves:
-                L = ml[i]
-                o = leaf_view(bucket, recv, i, sizes[i])
-                p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
-                items.append((o, p, L.out.view(-1), scales[i], decays[i]))
-            run_tail(items, lr, SIDE_CTAS_PER_SM)
-            if trace is not None:
-                trace.mark("tail", "tail_end")
+        tail(bucket, recv)
 
-    run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange, buffers)
-    for side in (comm, tail_stream):
-        done = torch.cuda.Event()
-        done.record(side)
-        compute.wait_event(done)
+    def exchange_ce(bucket, send, recv):
+        # Copy engines push this rank's slot to every peer while the compute
+        # stream moves on to the next bucket's GEMMs (no SMs taken).
+        ready = torch.cuda.Event()
+        ready.record(compute)
+        if trace is not None:
+            trace.mark("compute", "ns_end")
+        gather.push(bucket.index, ready)
+        if trace is not None:
+            trace.mark("comm", "push_end")
+
+    if gather is not None:
+        gather.begin_step()
+        run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange_ce, buffers)
+        # Tails after the last GEMM, at full occupancy on the compute stream:
+        # run beside the power-capped GEMMs, their HBM traffic slowed the
+        # GEMMs by more than it hid (8 B200s: GEMMs 49 -> 77 ms).  By now the
+        # earlier buckets have long arrived; only the last one's push can be
+        # exposed.
+        for b, (_, recv) in zip(plan.buckets, buffers):
+            gather.wait_bucket(b.index, compute)
+            with torch.cuda.stream(compute):
+                if trace is not None:
+                    trace.mark("compute", "tail")
+                items = []
+                for i in b.leaves:
+                    L = ml[i]
+                    p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+                    items.append((leaf_view(b, recv, i, sizes[i]), p, L.out.view(-1), scales[i], decays[i]))
+                run_tail(items, lr)
+        if trace is not None:
+            trace.mark("compute", "tail_end")
+        gather.end_step(compute, compute)
+    else:
+        run_buckets(plan, ctx.rank, ctx.world_size, sizes, compute_owned, exchange_nccl, buffers)
+        for side in (comm, tail_stream):
+            done = torch.cuda.Event()
+            done.record(side)
+            compute.wait_event(done)
     if trace is not None:
         trace.report(ctx.rank, [sum(sizes[i] for i in b.leaves) for b in plan.buckets])
     return _finish_leaves(ml)
+
+
+def active_transport(ctx: ShardContext | None = None) -> str:
+    """The transport the context's plans use: "ce", "nccl", or the configured
+    value when no plan has been built yet."""
+    ctx = ctx or _ctx
+    if ctx is None:
+        return "none"
+    kinds = {("ce" if e[2] is not None else "nccl") for e in ctx.plans.values()}
+    return kinds.pop() if len(kinds) == 1 else ctx.transport
 
 
 class _Trace:
@@ -300,7 +403,7 @@ class _Trace:
     synchronisation (diagnostics only; it serialises the host)."""
 
     def __init__(self, compute, comm):
-        self.streams = {"compute": compute, "comm": comm, "tail": _runtime.aux_stream(compute.device)}
+        self.streams = {"compute": compute, "comm": comm or compute, "tail": _runtime.aux_stream(compute.device)}
         self.marks = []
         self.t0 = torch.cuda.Event(enable_timing=True)
         self.t0.record(compute)

@@ -48,6 +48,7 @@ def test_bucket_layout_covers_every_leaf_once(world, buckets):
     costs = [ns_flops(1, *s) for s in leaves]
     plan = make_plan(sizes, costs, world, buckets)
     seen = [i for b in plan.buckets for i in b.leaves]
+    assert [b.index for b in plan.buckets] == list(range(len(plan.buckets)))
     assert seen == list(range(len(leaves)))
     assert len(plan.buckets) <= buckets
     for b in plan.buckets:
@@ -56,7 +57,7 @@ def test_bucket_layout_covers_every_leaf_once(world, buckets):
             r, off = b.offsets[i]
             assert r == plan.owner[i] and off == used[r]
             used[r] += sizes[i]
-        assert b.seg == max(used)
+        assert b.seg == -(-max(used) // 64) * 64 and b.used == used
     if len(plan.buckets) > 2:  # small last bucket: short exposed final gather
         bc = [sum(costs[i] for i in b.leaves) for b in plan.buckets]
         assert bc[-1] < max(bc)

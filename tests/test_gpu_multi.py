@@ -1,5 +1,6 @@
-"""Sharded Muon on 2 GPUs (NCCL): leaf ownership + all-gather must give the
-same updates as the unsharded single-GPU path.  Runs as child processes and
+"""Sharded Muon on 2 GPUs: leaf ownership + all-gather (copy-engine pushes
+into IPC-mapped peer buffers, and NCCL) must give the same updates as the
+unsharded single-GPU path, step after step.  Runs as child processes and
 needs >= 2 GPUs (skipped otherwise)."""
 
 import os
@@ -25,12 +26,13 @@ def _tree(dev, seed):
     return {k: torch.randn(s, device=dev, generator=g).to(torch.bfloat16) for k, s in shapes.items()}
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, transport, q):
     import datetime
 
     import torch.distributed as dist
 
     import rollfast_b200 as rf
+    from rollfast_b200 import _lib
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -47,17 +49,24 @@ def _worker(rank, world, port, q):
         ref_tx, sh_tx = rf.muon(**kw), rf.muon(**kw)
         ref_st, sh_st = ref_tx.init(params), sh_tx.init(params)
         ok = True
-        for step in range(2):
+        # One sharded context over three steps (the copy-engine epochs and
+        # acknowledgements advance), then a fresh context (mappings rebuilt).
+        ctx = rf.distributed.configure(buckets=2, transport=transport)
+        for step in range(4):
             grads = _tree(dev, 10 + step)
-            rf.distributed.clear()
+            if step == 3:
+                rf.distributed.clear()
+                ctx = rf.distributed.configure(buckets=3, transport=transport)
+            rf.distributed.use(None)                 # reference: the unsharded path
             u_ref, ref_st = ref_tx.update(grads, ref_st, params)
-            rf.distributed.configure(buckets=2)
+            rf.distributed.use(ctx)
             u_sh, sh_st = sh_tx.update(grads, sh_st, params)
-            rf.distributed.clear()
-            torch.cuda.synchronize()
+            _lib.sync_check(torch.cuda.current_stream().cuda_stream)  # no flag wait gave up
+            ok &= rf.distributed.active_transport(ctx) == transport
             for k in params:
                 e = float(torch.linalg.vector_norm(u_sh[k] - u_ref[k]) / torch.linalg.vector_norm(u_ref[k]))
                 ok &= e <= 2e-3  # 16-bit gathered O vs fused fp32 O
+        rf.distributed.clear()
         q.put((rank, ok))
     except Exception as exc:  # report instead of hanging the other rank
         q.put((rank, repr(exc)))
@@ -65,7 +74,8 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_sharded_update_matches_single_gpu_on_two_gpus():
+@pytest.mark.parametrize("transport", ["ce", "nccl"])
+def test_sharded_update_matches_single_gpu_on_two_gpus(transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -73,7 +83,7 @@ def test_sharded_update_matches_single_gpu_on_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in procs)
