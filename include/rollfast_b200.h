@@ -20,6 +20,10 @@
  *                              scale_by_learning_rate (src/rollfast/optim/adam.py:123-233, 380-404)
  *   rf_muon_tail            <- scale_by_shape + add_decayed_weights + scale_by_learning_rate
  *                              applied to gathered orthogonalised leaves (muon.py:130-137, 390-393, 466)
+ * Without a reference counterpart: rf_newton_schulz_noalloc (static
+ * workspace), and the peer transport of the multi-GPU sharded update
+ * (rf_ipc_*, rf_peer_copy, rf_flags_*; rf_ipc_open maps, but does not
+ * allocate, another process's memory).
  * A JAX integration registers these as XLA FFI custom calls; a ctypes
  * binding (rollfast_b200/_lib.py) is the host used in this repository.
  */

@@ -120,3 +120,52 @@ def test_gloo_world2_owner_compute_and_all_gather(buckets):
     for p in procs:
         p.join(timeout=60)
     assert results == {0: True, 1: True}
+
+
+def _configure_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    import rollfast_b200.distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        res = {}
+        try:
+            D.configure(transport="bogus")
+            res["bad"] = "accepted"
+        except ValueError:
+            res["bad"] = "rejected"
+        ctx = D.configure(transport="NCCL", buckets=3)
+        res["ctx"] = (ctx.rank, ctx.world_size, ctx.transport, ctx.buckets, D.active_transport())
+        prev = D.use(None)
+        res["use"] = (prev is ctx, D.current() is None, D.active_transport())
+        D.use(ctx)
+        os.environ["ROLLFAST_DIST_GATHER"] = "ce"
+        res["env"] = D.configure().transport
+        D.clear()
+        res["cleared"] = D.current() is None
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world2_configure_transport_selection():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_configure_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        res = results[r]
+        assert res["bad"] == "rejected"
+        assert res["ctx"] == (r, 2, "nccl", 3, "nccl")
+        assert res["use"] == (True, True, "none")
+        assert res["env"] == "ce" and res["cleared"]
