@@ -69,6 +69,14 @@ typedef struct rf_muon_leaf {
   int32_t skip_ns;    /* 1: this rank does not own the leaf (multi-GPU); momentum/NS skipped */
 } rf_muon_leaf;
 
+/* Newton-Schulz preconditioning (orthogonalization.py:24, 153-176, 233-250). */
+typedef enum rf_preconditioning {
+  RF_PRECOND_FROBENIUS = 0, /* X / (||X||_F + eps) */
+  RF_PRECOND_SPECTRAL = 1,  /* X / (||X||_2 + eps) */
+  RF_PRECOND_AOL = 2,       /* first iteration on diag(s) X, s_i = 1/sqrt(max(sum_j |(X X^T)_ij|, 1e-8)) */
+  RF_PRECOND_SCHATTEN = 3   /* first iteration on X / sqrt(max(||X X^T||_F, 1e-8)) */
+} rf_preconditioning;
+
 typedef struct rf_muon_params {
   float beta;            /* muon.py:402 */
   float eps;             /* muon.py:403, Frobenius normaliser epsilon */
@@ -94,6 +102,11 @@ typedef struct rf_muon_params {
   /* SMs the GEMM kernels leave free for concurrent kernels (e.g. a
    * collective or the tail on another stream); 0 = use every SM. */
   int32_t reserve_sms;
+  int32_t preconditioning;  /* rf_preconditioning (muon.py:410) */
+  /* 1: O <- <d, O> O per leaf before the tail (muon.py:272-282), d the
+   * Nesterov / bias-corrected direction; the NS final epilogue then writes O
+   * and a separate pass applies the factor and the tail. */
+  int32_t adaptive;
 } rf_muon_params;
 
 /* Bytes of workspace rf_muon_update needs for these leaves and precision
@@ -120,8 +133,8 @@ rf_status rf_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t c
                                           int32_t precision, size_t* bytes);
 rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
                            int64_t batch, int64_t rows, int64_t cols, const float* coeffs,
-                           int32_t n_coeff_rows, int32_t ns_steps, float eps, int32_t precision,
-                           void* workspace, size_t workspace_bytes, void* stream);
+                           int32_t n_coeff_rows, int32_t ns_steps, float eps, int32_t preconditioning,
+                           int32_t precision, void* workspace, size_t workspace_bytes, void* stream);
 
 /* rf_newton_schulz for callers that cannot allocate device memory (no
  * counterpart in the reference).  Hosts such as an XLA FFI handler, whose

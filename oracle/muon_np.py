@@ -342,12 +342,40 @@ def resolve_ns_coeffs(ns_coeffs, ns_steps) -> np.ndarray:
 # --------------------------------------------------------------------------
 
 
+PRECONDITIONINGS = ("frobenius", "spectral", "aol", "schatten")
+
+
+def _aol_first_iteration(m, a, b, c, dtype, clip=1e-8):
+    """orthogonalization.py:153-163.  The reference calls it without an
+    ``eps`` argument (189-192), so the clip is its default 1e-8."""
+    A = np.matmul(m, np.swapaxes(m, -1, -2))
+    rescaling = np.maximum(np.abs(A).sum(axis=-1), dtype(clip)).astype(dtype)
+    s = (dtype(1.0) / np.sqrt(rescaling)).astype(dtype)[..., :, None]
+    m = (m * s).astype(dtype)
+    A = (A * s * np.swapaxes(s, -1, -2)).astype(dtype)
+    B = b * A + c * np.matmul(A, A)
+    return (a * m + np.matmul(B, m)).astype(dtype)
+
+
+def _schatten_first_iteration(m, a, b, c, dtype, clip=1e-8):
+    """orthogonalization.py:166-176 (clip: its default 1e-8, as called at 198-201)."""
+    A = np.matmul(m, np.swapaxes(m, -1, -2))
+    fro = np.sqrt(np.sum(A * A, axis=(-2, -1), keepdims=True, dtype=dtype)).astype(dtype)
+    s = (dtype(1.0) / np.sqrt(np.maximum(fro, dtype(clip)))).astype(dtype)
+    m = (m * s).astype(dtype)
+    A = (A * s * s).astype(dtype)
+    B = b * A + c * np.matmul(A, A)
+    return (a * m + np.matmul(B, m)).astype(dtype)
+
+
 def quintic_newton_schulz(x: np.ndarray, ns_coeffs, ns_steps: int = 5, eps: float = 1e-8,
-                          dtype=np.float32) -> np.ndarray:
-    """orthogonalization.py:211-273 with ``preconditioning="frobenius"``.
+                          dtype=np.float32, preconditioning: str = "frobenius") -> np.ndarray:
+    """orthogonalization.py:211-273.
 
     Over the last two axes: cast (227), transpose when rows > cols (228-231),
-    X / (||X||_F + eps) per batch item (243-246), then for each step
+    then by ``preconditioning`` (233-250): "frobenius" X / (||X||_F + eps),
+    "spectral" X / (||X||_2 + eps), "aol" / "schatten" no pre-scaling but a
+    rescaled first iteration (153-176, 189-201).  Each step is
     A = X X^T, B = b A + c A A, X = a X + B X (179-182), with a (3,) array
     repeated ``ns_steps`` times (253-260) or an (n,3) schedule scanned in
     order (262-269); untranspose (271-272).
@@ -358,14 +386,27 @@ def quintic_newton_schulz(x: np.ndarray, ns_coeffs, ns_steps: int = 5, eps: floa
                          f"{coeffs.shape}.")
     if x.ndim < 2:
         raise ValueError(f"Input must have rank >= 2, got shape={x.shape}.")
+    if preconditioning not in PRECONDITIONINGS:
+        raise ValueError(f"Unknown preconditioning {preconditioning!r}.")
     m = np.asarray(x).astype(dtype)
     transposed = m.shape[-2] > m.shape[-1]
     if transposed:
         m = np.swapaxes(m, -1, -2)
-    norm = np.sqrt(np.sum(m.astype(dtype) * m, axis=(-2, -1), keepdims=True, dtype=dtype)).astype(dtype)
-    m = (m / (norm + dtype(eps))).astype(dtype)
+    if preconditioning == "frobenius":
+        norm = np.sqrt(np.sum(m.astype(dtype) * m, axis=(-2, -1), keepdims=True, dtype=dtype)).astype(dtype)
+        m = (m / (norm + dtype(eps))).astype(dtype)
+    elif preconditioning == "spectral":
+        # ord=2 matrix norm: the largest singular value (computed in float64 here).
+        sv = np.linalg.norm(m.astype(np.float64), ord=2, axis=(-2, -1), keepdims=True).astype(dtype)
+        m = (m / (sv + dtype(eps))).astype(dtype)
     schedule = [coeffs] * int(ns_steps) if coeffs.ndim == 1 else list(coeffs)
-    for a, b, c in schedule:
+    for i, (a, b, c) in enumerate(schedule):
+        if i == 0 and preconditioning == "aol":
+            m = _aol_first_iteration(m, a, b, c, dtype)
+            continue
+        if i == 0 and preconditioning == "schatten":
+            m = _schatten_first_iteration(m, a, b, c, dtype)
+            continue
         mt = np.swapaxes(m, -1, -2)
         A = np.matmul(m, mt)
         B = b * A + c * np.matmul(A, A)
@@ -377,17 +418,15 @@ def quintic_newton_schulz(x: np.ndarray, ns_coeffs, ns_steps: int = 5, eps: floa
 
 def orthogonalize_via_newton_schulz(x, ns_coeffs, ns_steps=5, preconditioning="frobenius",
                                     eps=1e-8, dimension_numbers=None, dtype=np.float32):
-    """orthogonalization.py:276-305 (frobenius preconditioning only)."""
+    """orthogonalization.py:276-305."""
     if is_aux_leaf(x):
         return x
-    if preconditioning != "frobenius":
-        raise NotImplementedError("oracle restates preconditioning='frobenius' only")
     if x.ndim != 2 and not isinstance(dimension_numbers, MatrixDimensionNumbers):
         raise ValueError("Input must have shape (m, n) or weight dimension numbers must be provided.")
     if x.ndim == 2:
         dimension_numbers = MatrixDimensionNumbers(0, 1)
     fwd, bwd = compute_matrix_reshape(x.shape, dimension_numbers)
-    return bwd(quintic_newton_schulz(fwd(x), ns_coeffs, ns_steps, eps, dtype))
+    return bwd(quintic_newton_schulz(fwd(x), ns_coeffs, ns_steps, eps, dtype, preconditioning))
 
 
 # --------------------------------------------------------------------------
@@ -477,7 +516,7 @@ def adam_leaf_update(g, mu, nu, count: int, *, b1=0.9, b2=0.999, eps=1e-8, eps_r
 
 class OracleMuon:
     """CPU restatement of ``rollfast.muon(...)`` for the options on the hot
-    path (no Magma, no adaptive, frobenius preconditioning, float32 state).
+    path (no Magma, float32 state; any preconditioning; ``adaptive``).
 
     ``params`` / ``grads`` are trees of float32 NumPy arrays; ``param_dtypes``
     (a matching tree of dtype names) tells the decay term which weak-typed
@@ -488,8 +527,10 @@ class OracleMuon:
                  weight_decay=0.0, weight_decay_mask=None, *, nesterov=True, adam_b1=0.9,
                  adam_b2=0.999, adam_eps=None, adam_eps_root=0.0, adam_weight_decay=None,
                  adam_learning_rate=None, muon_weight_dimension_numbers=None, consistent_rms=None,
-                 momentum_accumulator="ema", dtype=np.float32):
+                 momentum_accumulator="ema", preconditioning="frobenius", adaptive=False, dtype=np.float32):
         self.lr = learning_rate
+        self.preconditioning = preconditioning
+        self.adaptive = adaptive
         self.ns_coeffs = ns_coeffs
         self.ns_steps = ns_steps
         self.beta = beta
@@ -545,8 +586,10 @@ class OracleMuon:
                 mu_new, d = momentum_runtime(g, mu, count, self.beta, nesterov=self.nesterov,
                                              accumulator=self.acc, dtype=dt)
                 new_mu[key] = mu_new
-                o = orthogonalize_via_newton_schulz(d, coeffs, self.ns_steps, "frobenius", self.eps,
+                o = orthogonalize_via_newton_schulz(d, coeffs, self.ns_steps, self.preconditioning, self.eps,
                                                     spec, dtype=dt)
+                if self.adaptive:  # muon.py:272-282: <mu_hat, O> O over the whole leaf
+                    o = (np.sum(d.astype(dt) * o, dtype=dt) * o).astype(dt)
                 u = (o * shape_scale_factor(np.shape(g), spec, self.consistent_rms)).astype(dt)
                 if self.wd != 0.0 and msk:
                     u = (u + decay_term(p, self.wd, pdt)).astype(dt)

@@ -19,6 +19,9 @@ RF_OK, RF_EINVAL, RF_ECUDA, RF_ETIMEOUT, RF_ENOTSUP = 0, 1, 2, 3, 4
 RF_F32, RF_BF16, RF_F16 = 0, 1, 2
 RF_EMA, RF_HEAVY_BALL = 0, 1
 RF_NS_F16, RF_NS_BF16, RF_NS_F32 = 0, 1, 2
+RF_PRECOND_FROBENIUS, RF_PRECOND_SPECTRAL, RF_PRECOND_AOL, RF_PRECOND_SCHATTEN = 0, 1, 2, 3
+PRECONDITIONING_CODES = {"frobenius": RF_PRECOND_FROBENIUS, "spectral": RF_PRECOND_SPECTRAL,
+                         "aol": RF_PRECOND_AOL, "schatten": RF_PRECOND_SCHATTEN}
 
 PRECISIONS = {"f16": RF_NS_F16, "fp16": RF_NS_F16, "float16": RF_NS_F16,
               "bf16": RF_NS_BF16, "bfloat16": RF_NS_BF16,
@@ -86,6 +89,8 @@ class RfMuonParams(ctypes.Structure):
         ("fuse_tail", ctypes.c_int32),
         ("aux_stream", ctypes.c_void_p),
         ("reserve_sms", ctypes.c_int32),
+        ("preconditioning", ctypes.c_int32),
+        ("adaptive", ctypes.c_int32),
     ]
 
 
@@ -172,7 +177,7 @@ def load(path: str | None = None):
         lib.rf_muon_direction.argtypes = [ctypes.POINTER(RfMuonLeaf), i32, ctypes.POINTER(RfMuonParams), vp]
         lib.rf_newton_schulz_workspace_size.argtypes = [i64, i64, i64, i32, ctypes.POINTER(sz)]
         lib.rf_newton_schulz.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float), i32,
-                                         i32, ctypes.c_float, i32, vp, sz, vp]
+                                         i32, ctypes.c_float, i32, i32, vp, sz, vp]
         lib.rf_newton_schulz_noalloc.argtypes = [vp, i32, vp, i32, i64, i64, i64, ctypes.POINTER(ctypes.c_float),
                                                  i32, i32, ctypes.c_float, i32, vp]
         lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, i32, vp]

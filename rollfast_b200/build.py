@@ -16,7 +16,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "librollfast_b200.so")
-SOURCES = ["rf_api.cu", "rf_elementwise.cu", "rf_ns_simt.cu", "rf_ns_tc.cu", "rf_noalloc.cu", "rf_peer.cu"]
+SOURCES = ["rf_api.cu", "rf_elementwise.cu", "rf_ns_simt.cu", "rf_ns_tc.cu", "rf_noalloc.cu", "rf_peer.cu", "rf_precond.cu"]
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -245,8 +245,8 @@ struct EventPool {
 // on `st`.  With `aux`, sub-batch k+1's preparation overlaps sub-batch k's
 // GEMMs; workspace regions alternate, so preparing k+2 waits for k's GEMMs.
 static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
-                              int ns_steps, float eps, int fuse_tail, float lr, int reserve_sms, void* ws,
-                              size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
+                              int ns_steps, float eps, int precond, int fuse_tail, float lr, int reserve_sms,
+                              void* ws, size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
   if (P.leaves.empty()) return RF_OK;
   if (!ws || ws_bytes < P.bytes)
     return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
@@ -349,6 +349,35 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         RF_TRY(events.get(&ready));
         cudaEventRecord(ready, aux);
         cudaStreamWaitEvent(st, ready, 0);
+      }
+
+      // ---- preconditioning other than Frobenius (rf_precond.cu) ----
+      // A~ of the Frobenius-normalised operand gives the variant's scales
+      // (new per-matrix denominators, or per-row factors for aol); the
+      // operand is then loaded again with them.  The Lanczos basis lives in
+      // Bm and the small scratch in X1, both unused until iteration 1.
+      if (precond != RF_PRECOND_FROBENIUS && ns_steps > 0) {
+        ga.stage = kSyrkXXt;
+        ga.a_op = ga.b_op = X0;
+        ga.aux = nullptr;
+        ga.out = Am;
+        ga.alpha = sc.sa / (sc.sx * sc.sx);
+        ga.beta = 0.f;
+        RF_TRY(launch_ns_gemm(ga, st));
+        int64_t begins[kMaxLeavesPerLaunch], nidx[kMaxLeavesPerLaunch];
+        for (int i = 0; i < ld.n; ++i) {
+          begins[i] = ld.leaf[i].group_mat_begin;
+          nidx[i] = ld.leaf[i].norm_index;
+        }
+        const float* rows = nullptr;
+        RF_TRY(launch_precondition(precond, P.precision, Am, G, gp.m, gp.mp, sc.sa, begins, nidx, ld.n, denom, eps,
+                                   Bm, abytes, X1, xbytes, &rows, st));
+        ld.row_scale = rows;
+        for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
+          bool any = false;
+          for (int li : sub) any |= P.leaves[li].gdt == gdt;
+          if (any) RF_TRY(launch_ns_load(ld, gdt, P.precision, st));
+        }
       }
 
       // ---- Newton-Schulz GEMM stages on st ----
@@ -469,6 +498,63 @@ rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, i
   return RF_OK;
 }
 
+// adaptive (muon.py:272-282) after an unfused pipeline: `out` holds O; each
+// leaf's <d, O> goes to ip[] (the per-matrix scale slots, free once the NS
+// stages are queued), then out <- -lr (shape <d,O> O + decay p) in place, or
+// out <- <d,O> O without the tail.  Partial sums reuse the momentum partials.
+static rf_status adaptive_pass(const Plan& P, const MomentumCoeffs& mc, int fuse_tail, float lr, void* ws,
+                               cudaStream_t st) {
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  float* partials = reinterpret_cast<float*>(base + P.off_partials);
+  float* ip = reinterpret_cast<float*>(base + P.off_scale);
+  int64_t chunk_base = 0;
+  const int nl = int(P.leaves.size());
+  for (int s0 = 0; s0 < nl; s0 += kMaxLeavesPerLaunch) {
+    AdaptiveLaunch A{};
+    A.c = mc;
+    A.partials = partials + chunk_base;
+    TailLaunch T{};
+    T.neg_lr = fuse_tail ? -lr : 1.f;
+    int64_t chunks = 0;
+    for (int i = s0; i < std::min(nl, s0 + kMaxLeavesPerLaunch); ++i) {
+      const LeafPlan& lp = P.leaves[i];
+      const int64_t n = lp.batch * lp.rows * lp.cols;
+      AdaptiveLeaf& a = A.leaf[A.n++];
+      a.g = lp.g;
+      a.mu = lp.mu;
+      a.o = lp.out;
+      a.n = n;
+      a.chunk_begin = chunks;
+      a.gdt = lp.gdt;
+      a.odt = lp.odt;
+      TailLeafDev& t = T.leaf[T.n++];
+      t.o = lp.out;
+      t.p = fuse_tail ? lp.p : nullptr;
+      t.out = lp.out;
+      t.n = n;
+      t.chunk_begin = chunks;
+      t.odt = t.outdt = lp.odt;
+      t.pdt = lp.p ? lp.pdt : RF_F32;
+      t.shape_scale = fuse_tail ? lp.shape_scale : 1.f;
+      t.decay = fuse_tail ? lp.decay : 0.f;
+      t.dev_scale = ip + i;
+      t.vec_ok = (n % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
+                 (!t.p || reinterpret_cast<uintptr_t>(lp.p) % 16 == 0);
+      chunks += ceil_div(n, kChunk);
+    }
+    A.total_chunks = T.total_chunks = chunks;
+    for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
+      bool any = false;
+      for (int k = 0; k < A.n; ++k) any |= A.leaf[k].gdt == gdt;
+      if (any) RF_TRY(launch_adaptive_dot(A, gdt, st));
+    }
+    RF_TRY(launch_adaptive_finalize(A, ip + s0, st));
+    RF_TRY(launch_tail(T, st));
+    chunk_base += chunks;
+  }
+  return RF_OK;
+}
+
 rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
                          void* workspace, size_t workspace_bytes, void* stream) {
   if (!params) return fail(RF_EINVAL, "null params");
@@ -485,7 +571,17 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   RF_TRY(leaves_from_abi(leaves, n_leaves, lp, true));
   Plan P;
   RF_TRY(build_plan(lp, p.precision, P, p.aux_stream ? 2 : 1));
-  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.fuse_tail, p.lr,
+  if (p.preconditioning < RF_PRECOND_FROBENIUS || p.preconditioning > RF_PRECOND_SCHATTEN)
+    return fail(RF_EINVAL, "unknown preconditioning");
+  if (p.adaptive) {
+    const MomentumCoeffs mc = momentum_coeffs(p);
+    RF_TRY(run_pipeline(P, mc, p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 0, 0.f, p.reserve_sms,
+                        workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                        static_cast<cudaStream_t>(p.aux_stream)));
+    return adaptive_pass(P, mc, p.fuse_tail, p.lr, workspace, static_cast<cudaStream_t>(stream));
+  }
+  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning,
+                      p.fuse_tail, p.lr,
                       p.reserve_sms, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                       static_cast<cudaStream_t>(p.aux_stream));
 }
@@ -561,8 +657,11 @@ rf_status rf_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t c
 
 rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t out_dtype, int64_t batch,
                            int64_t rows, int64_t cols, const float* coeffs, int32_t n_coeff_rows, int32_t ns_steps,
-                           float eps, int32_t precision, void* workspace, size_t workspace_bytes, void* stream) {
+                           float eps, int32_t preconditioning, int32_t precision, void* workspace,
+                           size_t workspace_bytes, void* stream) {
   if (!x || !out) return fail(RF_EINVAL, "x and out must be non-null");
+  if (preconditioning < RF_PRECOND_FROBENIUS || preconditioning > RF_PRECOND_SCHATTEN)
+    return fail(RF_EINVAL, "unknown preconditioning");
   if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype)) return fail(RF_EINVAL, "bad dtype");
   if (!(eps > 0.f)) return fail(RF_EINVAL, "eps must be positive");
   int iters = 0;
@@ -571,7 +670,7 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
   RF_TRY(ns_plan(batch, rows, cols, precision, P, x, x_dtype, out, out_dtype));
   MomentumCoeffs mc{};
   mc.mode = kDirIdentity;
-  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, 0, 0.f, 0, workspace, workspace_bytes,
+  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, preconditioning, 0, 0.f, 0, workspace, workspace_bytes,
                       static_cast<cudaStream_t>(stream), nullptr);
 }
 

@@ -296,12 +296,13 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
     // sx / (||d|| + eps): one division per tile; sx is a power of two.
     const float scale = P.sx / P.denom[L.norm_index + bi];
     OT* out = static_cast<OT*>(P.x) + gm * P.mp * P.np;
+    const float* rs = P.row_scale ? P.row_scale + gm * P.mp : nullptr;
     if (!L.transposed) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int64_t r = r0 + tr + 32 * h;
         float v[8];
-        dir8<GDT>(P, L, base, r, c0 + tc, scale, v);
+        dir8<GDT>(P, L, base, r, c0 + tc, rs ? P.sx * rs[r] : scale, v);
         store8<OT>(out + r * P.np + c0 + tc, v);
       }
     } else {
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
       for (int h = 0; h < 2; ++h) {
         const int lr = tr + 32 * h;
         float v[8];
-        dir8<GDT>(P, L, base, c0 + lr, r0 + tc, scale, v);
+        dir8<GDT>(P, L, base, c0 + lr, r0 + tc, rs ? P.sx : scale, v);
 #pragma unroll
         for (int k = 0; k < 8; ++k) tile[lr][tc + k] = v[k];
       }
@@ -320,8 +321,11 @@ __global__ void __launch_bounds__(256) k_ns_load(const __grid_constant__ LoadLau
       for (int h = 0; h < 2; ++h) {
         const int orow = tr + 32 * h;
         float v[8];
+        // With row factors, sx (a power of two) was applied exactly above and
+        // the factor rounds once here, as in the untransposed branch.
+        const float f = rs ? rs[r0 + orow] : 1.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = tile[tc + k][orow];
+        for (int k = 0; k < 8; ++k) v[k] = rs ? tile[tc + k][orow] * f : tile[tc + k][orow];
         store8<OT>(out + (r0 + orow) * P.np + c0 + tc, v);
       }
     }
@@ -426,8 +430,9 @@ __global__ void __launch_bounds__(kEwThreads) k_direction(const __grid_constant_
 // ---------------------------------------------------------------------------
 // k_tail: out = -lr * (shape_scale * O + decay * p) for gathered leaves.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float tail_one(const TailLeafDev& L, float neg_lr, float o, float p) {
-  float u = __fmul_rn(o, L.shape_scale);
+// ds: the adaptive factor <d, O> (1 otherwise, which leaves o unchanged).
+__device__ __forceinline__ float tail_one(const TailLeafDev& L, float neg_lr, float o, float p, float ds) {
+  float u = __fmul_rn(__fmul_rn(ds, o), L.shape_scale);
   if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.pdt, L.decay, p));
   return __fmul_rn(neg_lr, u);
 }
@@ -441,22 +446,58 @@ __global__ void __launch_bounds__(kEwThreads) k_tail(const __grid_constant__ Tai
     const TailLeafDev& L = P.leaf[li];
     const int64_t lo = (chunk - L.chunk_begin) * kChunk;
     const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    const float ds = L.dev_scale ? *L.dev_scale : 1.f;
     if (L.vec_ok) {
       for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
         float o[8], p[8], u[8];
         ld8(L.o, L.odt, i, o);
         if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) u[k] = tail_one(L, P.neg_lr, o[k], L.decay != 0.f ? p[k] : 0.f);
+        for (int k = 0; k < 8; ++k) u[k] = tail_one(L, P.neg_lr, o[k], L.decay != 0.f ? p[k] : 0.f, ds);
         st8(L.out, L.outdt, i, u);
       }
     } else {
       for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
-        st_from_float(L.out, L.outdt, i, tail_one(L, P.neg_lr, ld_as_float(L.o, L.odt, i), p));
+        st_from_float(L.out, L.outdt, i, tail_one(L, P.neg_lr, ld_as_float(L.o, L.odt, i), p, ds));
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// adaptive (muon.py:272-282): per-chunk partial sums of d * O over each leaf
+// (d with the reference's exact float32 direction formula), then one
+// fixed-order sum per leaf.
+// ---------------------------------------------------------------------------
+template <int GDT>
+__global__ void __launch_bounds__(kEwThreads) k_adaptive_dot(const __grid_constant__ AdaptiveLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  __shared__ float red[32];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const AdaptiveLeaf& L = P.leaf[find_leaf(s_begin, P.n, chunk)];
+    if (L.gdt != GDT) continue;  // uniform per chunk: another launch covers it
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    float s = 0.f;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+      s += direction(P.c, ld_as_float(L.g, GDT, i), L.mu[i]) * ld_as_float(L.o, L.odt, i);
+    s = block_sum(s, red);
+    if (threadIdx.x == 0) P.partials[chunk] = s;
+  }
+}
+
+__global__ void __launch_bounds__(kEwThreads) k_adaptive_finalize(const __grid_constant__ AdaptiveLaunch P,
+                                                                  float* ip) {
+  __shared__ float red[32];
+  const AdaptiveLeaf& L = P.leaf[blockIdx.x];
+  const int64_t nch = (L.n + kChunk - 1) / kChunk;
+  float s = 0.f;
+  for (int64_t k = threadIdx.x; k < nch; k += blockDim.x) s += P.partials[L.chunk_begin + k];
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) ip[blockIdx.x] = s;
 }
 
 // ---------------------------------------------------------------------------
@@ -509,6 +550,21 @@ rf_status launch_direction(const DirLaunch& P, cudaStream_t st) {
   if (P.total_chunks == 0) return RF_OK;
   k_direction<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
   return check_launch("k_direction");
+}
+
+rf_status launch_adaptive_dot(const AdaptiveLaunch& P, int gdt, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  const int grid = ew_grid(P.total_chunks);
+  if (gdt == RF_F32) k_adaptive_dot<RF_F32><<<grid, kEwThreads, 0, st>>>(P);
+  else if (gdt == RF_BF16) k_adaptive_dot<RF_BF16><<<grid, kEwThreads, 0, st>>>(P);
+  else k_adaptive_dot<RF_F16><<<grid, kEwThreads, 0, st>>>(P);
+  return check_launch("k_adaptive_dot");
+}
+
+rf_status launch_adaptive_finalize(const AdaptiveLaunch& P, float* ip, cudaStream_t st) {
+  if (P.n == 0) return RF_OK;
+  k_adaptive_finalize<<<P.n, kEwThreads, 0, st>>>(P, ip);
+  return check_launch("k_adaptive_finalize");
 }
 
 rf_status launch_tail(const TailLaunch& P, cudaStream_t st) {

@@ -69,6 +69,9 @@ struct LoadLaunch {
   float sx;            // power-of-two operand scale of this group
   void* x;             // X~0 for matrix 0 of this launch
   MomentumCoeffs c;
+  // Optional [group_mats][mp] per-operand-row factors replacing 1 / denom
+  // (AOL preconditioning); null: one denominator per matrix.
+  const float* row_scale;
 };
 
 struct AdamCoeffs {
@@ -117,6 +120,7 @@ struct TailLeafDev {
   int32_t odt, pdt, outdt;
   int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
   float shape_scale, decay;
+  const float* dev_scale;  // optional device factor applied to O first (adaptive)
 };
 struct TailLaunch {
   TailLeafDev leaf[kMaxLeavesPerLaunch];
@@ -172,6 +176,35 @@ rf_status launch_norm_finalize(const MomentumLaunch& P, float* denom, float eps,
 rf_status launch_ns_load(const LoadLaunch& P, int gdt, int precision, cudaStream_t st);
 rf_status launch_adamw(const AdamLaunch& P, cudaStream_t st);
 rf_status launch_tail(const TailLaunch& P, cudaStream_t st);
+
+// adaptive (muon.py:272-282): per leaf <d, O> over the whole leaf, d the
+// Nesterov / bias-corrected direction recomputed from g and the updated mu.
+struct AdaptiveLeaf {
+  const void* g;
+  const float* mu;
+  const void* o;
+  int64_t n, chunk_begin;
+  int32_t gdt, odt;
+};
+struct AdaptiveLaunch {
+  AdaptiveLeaf leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  MomentumCoeffs c;
+  float* partials;  // [total_chunks]
+};
+rf_status launch_adaptive_dot(const AdaptiveLaunch& P, int gdt, cudaStream_t st);
+rf_status launch_adaptive_finalize(const AdaptiveLaunch& P, float* ip, cudaStream_t st);
+
+// Preconditioning variants (rf_precond.cu).  Reads A~ = sa X_F X_F^T of one
+// sub-batch and either rewrites the per-matrix denominators (schatten,
+// spectral) or returns per-row factors in `scratch` (aol, *row_scale).
+// `basis` holds the Lanczos vectors (spectral): G * (min(64, m) + 1) * mp floats.
+size_t precondition_scratch_bytes(int64_t G, int64_t mp);
+rf_status launch_precondition(int mode, int precision, const void* A, int64_t G, int64_t m, int64_t mp, float sa,
+                              const int64_t* begins, const int64_t* norm_index, int n_leaves, float* denom,
+                              float eps, void* basis, size_t basis_bytes, void* scratch, size_t scratch_bytes,
+                              const float** row_scale, cudaStream_t st);
 rf_status launch_direction(const DirLaunch& P, cudaStream_t st);
 
 // NS GEMM stage: tcgen05 path for 16-bit operands, SIMT path for fp32 (or

@@ -73,5 +73,5 @@ extern "C" rf_status rf_newton_schulz_noalloc(const void* x, int32_t x_dtype, vo
   void* ws = nullptr;
   RF_TRY(scratch_for_current_device(&ws));
   return rf_newton_schulz(x, x_dtype, out, out_dtype, batch, rows, cols, coeffs, n_coeff_rows, ns_steps, eps,
-                          precision, ws, kStaticScratchBytes, stream);
+                          RF_PRECOND_FROBENIUS, precision, ws, kStaticScratchBytes, stream);
 }

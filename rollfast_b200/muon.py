@@ -181,7 +181,8 @@ def _leaf_table(ml: list, scales, decays):
     return arr
 
 
-def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail, reserve_sms=0):
+def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail, reserve_sms=0,
+                 preconditioning: str = "frobenius", adaptive: bool = False):
     cbuf, rows = coeff_buffer(ns_coeffs)
     prm = _lib.RfMuonParams()
     prm.beta = float(beta)
@@ -197,6 +198,8 @@ def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps
     prm.fuse_tail = int(fuse_tail)
     prm.aux_stream = None
     prm.reserve_sms = int(reserve_sms)
+    prm.preconditioning = _lib.PRECONDITIONING_CODES[preconditioning]
+    prm.adaptive = int(bool(adaptive))
     return prm, cbuf
 
 
@@ -273,14 +276,13 @@ _resolve_ns_coeffs = resolve_ns_coeffs
 def _check_supported(*, adaptive, preconditioning, use_magma, mu_dtype, orthogonalize_fn):
     if use_magma:
         raise NotImplementedError("Magma masking is not on the B200 hot path")
-    if adaptive:
-        raise NotImplementedError("adaptive=True is not on the B200 hot path")
+    if adaptive and orthogonalize_fn is not orthogonalize_via_newton_schulz:
+        raise NotImplementedError("adaptive=True with a custom orthogonalize_fn is not supported "
+                                  "(the default Newton-Schulz path computes <mu_hat, O> on the GPU)")
     if mu_dtype is not None and mu_dtype not in (torch.float32, "float32", "f32"):
         raise NotImplementedError("mu_dtype other than float32 (stochastic-rounding bf16 state) is not supported")
     if preconditioning not in ("frobenius", "spectral", "aol", "schatten"):
         raise ValueError(f"Unknown preconditioning {preconditioning!r}.")
-    if preconditioning != "frobenius" and orthogonalize_fn is orthogonalize_via_newton_schulz:
-        raise NotImplementedError(f"preconditioning={preconditioning!r} is not on the B200 hot path")
 
 
 def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8, mu_dtype=None, *,
@@ -322,7 +324,7 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
         ml = _gather_muon_leaves(leaves, mus, None, specs, "scale_by_muon")
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=count, nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=state.ns_coeffs, ns_steps=ns_steps,
-                                 lr=0.0, fuse_tail=0)
+                                 lr=0.0, fuse_tail=0, preconditioning=preconditioning, adaptive=adaptive)
         ones, zeros = [1.0] * len(ml), [0.0] * len(ml)
         if orthogonalize_fn is orthogonalize_via_newton_schulz:
             _run_muon_update(ml, prm, cbuf, ones, zeros)
@@ -444,7 +446,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
                                  ns_steps=ns_steps, lr=lr, fuse_tail=1,
-                                 reserve_sms=ctx.reserve_sms if (ctx is not None and ctx.world_size > 1) else 0)
+                                 reserve_sms=ctx.reserve_sms if (ctx is not None and ctx.world_size > 1) else 0,
+                                 preconditioning=preconditioning, adaptive=adaptive)
         if ctx is not None and ctx.world_size > 1:
             outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr)
         else:

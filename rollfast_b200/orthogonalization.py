@@ -129,13 +129,10 @@ def quintic_newton_schulz(x: torch.Tensor, ns_coeffs: torch.Tensor, ns_steps: in
                           preconditioning: MuonPreconditioning = "frobenius", eps: float = 1e-8,
                           *, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """orthogonalization.py:211-273 over the last two axes of ``x`` (fp32
-    output, like the reference's float32 iteration)."""
+    output, like the reference's float32 iteration), with any of the
+    reference's preconditionings (frobenius, spectral, aol, schatten)."""
     if preconditioning not in _PRECONDITIONINGS:
         raise ValueError(f"Unknown preconditioning {preconditioning!r}.")
-    if preconditioning != "frobenius":
-        raise NotImplementedError(
-            f"preconditioning={preconditioning!r} is not on the B200 hot path (frobenius only)"
-        )
     if x.ndim < 2:
         raise ValueError(f"Input must have rank >= 2, got shape={tuple(x.shape)}.")
     require_cuda(x, "x")
@@ -152,7 +149,8 @@ def quintic_newton_schulz(x: torch.Tensor, ns_coeffs: torch.Tensor, ns_steps: in
     _lib.check(lib.rf_newton_schulz_workspace_size(batch, r, c, prec, ctypes.byref(nbytes)))
     ws = _runtime.workspace(xc.device, nbytes.value)
     _lib.check(lib.rf_newton_schulz(xc.data_ptr(), rf_dtype(xc), out.data_ptr(), rf_dtype(out), batch, r, c,
-                                    cbuf, rows, int(ns_steps), float(eps), prec, ws.data_ptr(), ws.numel(),
+                                    cbuf, rows, int(ns_steps), float(eps),
+                                    _lib.PRECONDITIONING_CODES[preconditioning], prec, ws.data_ptr(), ws.numel(),
                                     stream_handle(xc)))
     return out
 

@@ -152,8 +152,10 @@ def test_adamw_rejects_negative_weight_decay():
 def test_unsupported_options_fail_loudly():
     with pytest.raises(NotImplementedError):
         rf.scale_by_muon(use_magma=True)
-    with pytest.raises(NotImplementedError):
-        rf.scale_by_muon(preconditioning="spectral")
+    with pytest.raises(ValueError, match="Unknown preconditioning"):
+        rf.scale_by_muon(preconditioning="nuclear")
+    with pytest.raises(NotImplementedError, match="adaptive"):
+        rf.scale_by_muon(adaptive=True, orthogonalize_fn=lambda x, *a: x)
     with pytest.raises(NotImplementedError):
         rf.muon(learning_rate=0.1, mu_dtype=torch.bfloat16)
 

@@ -244,3 +244,76 @@ def test_fp32_newton_schulz_close_to_fp64_truth():
     a = O.quintic_newton_schulz(x, c, 5, dtype=np.float32)
     b = O.quintic_newton_schulz(x, c, 5, dtype=np.float64)
     assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# Preconditioning variants (orthogonalization.py:153-176, 233-250).  On a
+# scaled identity or a diagonal matrix every iteration acts on each singular
+# value as sigma -> a sigma + b sigma^3 + c sigma^5, which gives closed forms.
+# ---------------------------------------------------------------------------
+
+
+def _scalar_ns(sigma, coeffs, steps):
+    a, b, c = (float(v) for v in coeffs)
+    for _ in range(steps):
+        sigma = a * sigma + b * sigma ** 3 + c * sigma ** 5
+    return sigma
+
+
+def test_schatten_scales_first_iterate_by_the_fourth_root():
+    # ||(3I)(3I)^T||_F = 9 * sqrt(4) = 18, so X / sqrt(18) = I / sqrt(2).
+    c = O.MUON_NS_COEFFS
+    out = O.quintic_newton_schulz(3.0 * np.eye(4), c, 3, dtype=np.float64, preconditioning="schatten")
+    np.testing.assert_allclose(out, _scalar_ns(1 / np.sqrt(2.0), c, 3) * np.eye(4), rtol=1e-12, atol=1e-14)
+
+
+def test_aol_maps_a_diagonal_matrix_to_its_signs():
+    # A = D^2, row sums d_i^2, s_i = 1/|d_i|: the first iterate is sign(D).
+    d = np.array([4.0, -0.5, 2.0, 9.0])
+    c = O.MUON_NS_COEFFS
+    out = O.quintic_newton_schulz(np.diag(d), c, 2, dtype=np.float64, preconditioning="aol")
+    np.testing.assert_allclose(out, _scalar_ns(1.0, c, 2) * np.diag(np.sign(d)), rtol=1e-12, atol=1e-14)
+
+
+def test_spectral_divides_by_the_largest_singular_value():
+    d = np.array([4.0, -0.5, 2.0, 8.0])
+    c = O.MUON_NS_COEFFS
+    out = O.quintic_newton_schulz(np.diag(d), c, 4, eps=1e-8, dtype=np.float64, preconditioning="spectral")
+    want = np.diag([np.sign(v) * _scalar_ns(abs(v) / (8.0 + 1e-8), c, 4) for v in d])
+    np.testing.assert_allclose(out, want, rtol=1e-10, atol=1e-14)
+
+
+def test_reference_schatten_mode_runs_case():
+    # test_muon.py:358-368: arange(1..16) 4x4, polar express 2 steps.
+    mat = np.arange(1, 17, dtype=np.float32).reshape(4, 4)
+    out = O.orthogonalize_via_newton_schulz(mat, np.asarray(O.polar_express_coeffs(num_iters=2)), ns_steps=2,
+                                            preconditioning="schatten",
+                                            dimension_numbers=O.MatrixDimensionNumbers())
+    assert out.shape == mat.shape and np.all(np.isfinite(out))
+
+
+def test_unknown_preconditioning_is_rejected():
+    with pytest.raises(ValueError, match="Unknown preconditioning"):
+        O.quintic_newton_schulz(np.eye(3), O.MUON_NS_COEFFS, 1, preconditioning="nuclear")
+
+
+@pytest.mark.parametrize("shape", [(24, 40), (40, 24), (2, 16, 48)])
+def test_aol_and_schatten_equal_rescaled_standard_iterations(shape):
+    """The CUDA path's reformulation: the rescaled first iteration equals the
+    standard iteration applied to diag(s) X (aol) or s X (schatten), where s
+    comes from A = X X^T of the raw matrix."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal(shape) * 3.0
+    c = O.MUON_NS_COEFFS
+    m = np.swapaxes(x, -1, -2) if shape[-2] > shape[-1] else x
+    A = m @ np.swapaxes(m, -1, -2)
+    s_row = 1.0 / np.sqrt(np.maximum(np.abs(A).sum(-1), 1e-8))[..., :, None]
+    s_mat = 1.0 / np.sqrt(np.maximum(np.sqrt((A * A).sum(axis=(-2, -1), keepdims=True)), 1e-8))
+    for pre, scaled in (("aol", m * s_row), ("schatten", m * s_mat)):
+        got = O.quintic_newton_schulz(x, c, 4, dtype=np.float64, preconditioning=pre)
+        y = scaled
+        for _ in range(4):
+            B = c[1] * (y @ np.swapaxes(y, -1, -2)) + c[2] * np.linalg.matrix_power(y @ np.swapaxes(y, -1, -2), 2)
+            y = c[0] * y + B @ y
+        want = np.swapaxes(y, -1, -2) if shape[-2] > shape[-1] else y
+        np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)

@@ -26,7 +26,7 @@ def _call_existing(lib, _lib, x, out, coeffs, rows, prec, stream):
     _lib.check(lib.rf_newton_schulz_workspace_size(b, r, c, prec, ctypes.byref(n)))
     ws = torch.empty(n.value, dtype=torch.uint8, device=x.device)
     _lib.check(lib.rf_newton_schulz(x.data_ptr(), _lib.RF_F32, out.data_ptr(), _lib.RF_F32, b, r, c, coeffs, rows,
-                                    5, 1e-8, prec, ws.data_ptr(), ws.numel(), stream))
+                                    5, 1e-8, _lib.RF_PRECOND_FROBENIUS, prec, ws.data_ptr(), ws.numel(), stream))
     return ws
 
 
