@@ -20,6 +20,7 @@
  *                              scale_by_learning_rate (src/rollfast/optim/adam.py:123-233, 380-404)
  *   rf_muon_tail            <- scale_by_shape + add_decayed_weights + scale_by_learning_rate
  *                              applied to gathered orthogonalised leaves (muon.py:130-137, 390-393, 466)
+ *   rf_apply_updates        <- apply_updates with bf16 stochastic rounding (src/rollfast/utils.py:342-371, 648-708)
  * Without a reference counterpart: rf_newton_schulz_noalloc (static
  * workspace), and the peer transport of the multi-GPU sharded update
  * (rf_ipc_*, rf_peer_copy, rf_flags_*; rf_ipc_open maps, but does not
@@ -198,6 +199,24 @@ typedef struct rf_adam_params {
 } rf_adam_params;
 rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
                           void* stream);
+
+/* Parameter apply p <- p + u (utils.py:648-708): the sum in float32, then
+ * the parameter dtype.  bfloat16 parameters round stochastically when
+ * `stochastic` (utils.py:342-371: 16 random bits are added below the bf16
+ * significand, then truncated; +-Inf and NaN get no noise), else to nearest
+ * even; other dtypes round to nearest even.  The random bits are the
+ * SplitMix64 sequence seeded with the leaf's `seed` (16 bits per element,
+ * in element order); the reference draws them from JAX's Threefry stream, so
+ * the two agree in distribution, not bit for bit.  `out` may alias `param`. */
+typedef struct rf_apply_leaf {
+  const void* param;   /* [n], param_dtype */
+  const void* update;  /* [n], update_dtype */
+  void* out;           /* [n], param_dtype */
+  int64_t n;
+  int32_t param_dtype, update_dtype;
+  uint64_t seed;
+} rf_apply_leaf;
+rf_status rf_apply_updates(const rf_apply_leaf* leaves, int32_t n_leaves, int32_t stochastic, void* stream);
 
 /* ------------------------------------------------------------------------
  * Peer transport for the multi-GPU Muon update (one process per GPU, one

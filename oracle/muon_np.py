@@ -22,6 +22,11 @@ from typing import Any, Callable, NamedTuple, Sequence
 import numpy as np
 
 __all__ = [
+    "PRECONDITIONINGS",
+    "apply_updates",
+    "noise16",
+    "splitmix64",
+    "stochastic_round_bf16",
     "MaskedNode",
     "MatrixDimensionNumbers",
     "MUON_NS_COEFFS",
@@ -427,6 +432,59 @@ def orthogonalize_via_newton_schulz(x, ns_coeffs, ns_steps=5, preconditioning="f
         dimension_numbers = MatrixDimensionNumbers(0, 1)
     fwd, bwd = compute_matrix_reshape(x.shape, dimension_numbers)
     return bwd(quintic_newton_schulz(fwd(x), ns_coeffs, ns_steps, eps, dtype, preconditioning))
+
+
+# --------------------------------------------------------------------------
+# Parameter apply (utils.py:342-371, 648-708).
+# --------------------------------------------------------------------------
+_GAMMA = np.uint64(0x9E3779B97F4A7C15)
+
+
+def splitmix64(state: np.ndarray) -> np.ndarray:
+    """SplitMix64 output for each 64-bit state (Steele, Lea and Flood, 2014):
+    z = state + gamma, then the two xor-shift-multiply rounds."""
+    with np.errstate(over="ignore"):
+        z = np.asarray(state, np.uint64) + _GAMMA
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def noise16(seed: int, n: int) -> np.ndarray:
+    """The library's 16-bit rounding noise for elements 0..n-1 of a leaf:
+    SplitMix64 output c (state seed + c * gamma) feeds elements 4c..4c+3,
+    16 bits each from the low end.  (The reference uses JAX Threefry bits
+    here, which cannot be reproduced without JAX.)"""
+    c = np.arange((n + 3) // 4, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        r = splitmix64(np.uint64(seed) + c * _GAMMA)
+    parts = [(r >> np.uint64(16 * k)) & np.uint64(0xFFFF) for k in range(4)]
+    return np.stack(parts, axis=1).reshape(-1)[:n].astype(np.uint32)
+
+
+def stochastic_round_bf16(x: np.ndarray, noise: np.ndarray) -> np.ndarray:
+    """utils.py:342-371 with given 16-bit noise: add it to the float32 bits
+    (none for +-Inf / NaN), clear the low 16 bits; returns float32 arrays
+    holding bfloat16 values."""
+    b = np.ascontiguousarray(np.asarray(x, np.float32)).view(np.uint32)
+    special = (b & np.uint32(0x7FFFFFFF)) >= np.uint32(0x7F800000)
+    n = np.where(special, np.uint32(0), np.asarray(noise, np.uint32) & np.uint32(0xFFFF))
+    return ((b + n) & np.uint32(0xFFFF0000)).astype(np.uint32).view(np.float32)
+
+
+def apply_updates(p: np.ndarray, u: np.ndarray, param_dtype: str, *, stochastic: bool = False,
+                  seed: int = 0) -> np.ndarray:
+    """utils.py:648-708 for one leaf (float32 arrays carrying the stored
+    values): the sum in float32, then the parameter dtype; bfloat16 rounds
+    stochastically (noise16(seed)) or to nearest even."""
+    total = (np.asarray(p, np.float32) + np.asarray(u, np.float32)).astype(np.float32)
+    if param_dtype == "bfloat16":
+        if stochastic:
+            return stochastic_round_bf16(total, noise16(seed, total.size).reshape(total.shape))
+        return bf16_round(total)
+    if param_dtype == "float16":
+        return f16_round(total)
+    return total
 
 
 # --------------------------------------------------------------------------

@@ -43,6 +43,7 @@ EXPORTED = (
     "rf_sync_check",
     "rf_profile_begin",
     "rf_profile_end",
+    "rf_apply_updates",
     "rf_ipc_export",
     "rf_ipc_open",
     "rf_ipc_close",
@@ -50,6 +51,18 @@ EXPORTED = (
     "rf_flags_signal",
     "rf_flags_wait",
 )
+
+
+class RfApplyLeaf(ctypes.Structure):
+    _fields_ = [
+        ("param", ctypes.c_void_p),
+        ("update", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("n", ctypes.c_int64),
+        ("param_dtype", ctypes.c_int32),
+        ("update_dtype", ctypes.c_int32),
+        ("seed", ctypes.c_uint64),
+    ]
 
 
 class RfIpcHandle(ctypes.Structure):
@@ -182,6 +195,7 @@ def load(path: str | None = None):
                                                  i32, i32, ctypes.c_float, i32, vp]
         lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, i32, vp]
         lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
+        lib.rf_apply_updates.argtypes = [ctypes.POINTER(RfApplyLeaf), i32, i32, vp]
         lib.rf_ipc_export.argtypes = [vp, ctypes.POINTER(RfIpcHandle), ctypes.POINTER(sz)]
         lib.rf_ipc_open.argtypes = [ctypes.POINTER(RfIpcHandle), ctypes.POINTER(vp)]
         lib.rf_ipc_close.argtypes = [vp]

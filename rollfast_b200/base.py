@@ -321,11 +321,67 @@ def add_decayed_weights(weight_decay: float = 0.0, mask=None) -> GradientTransfo
     return tx
 
 
-def apply_updates(params, updates):
-    """optax.apply_updates (outside the timed step; provided for examples)."""
-    return tree_map(
-        lambda p, u: p if is_aux_leaf(u) else (p.float() + u.float()).to(p.dtype),
-        params,
-        updates,
-        is_leaf=is_aux_leaf,
-    )
+def _splitmix64(x: int) -> int:
+    """One SplitMix64 output for state ``x`` (Steele, Lea and Flood, 2014)."""
+    m = (1 << 64) - 1
+    z = (x + 0x9E3779B97F4A7C15) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    return z ^ (z >> 31)
+
+
+def key_seed(key) -> int:
+    """64-bit seed of a PRNG key: an int, or a 2-element tensor / sequence of
+    32-bit words like ``jax.random.PRNGKey`` (``fresh_key`` layout)."""
+    if isinstance(key, int):
+        return key & ((1 << 64) - 1)
+    words = [int(v) & 0xFFFFFFFF for v in (key.reshape(-1).tolist() if isinstance(key, torch.Tensor) else key)]
+    if len(words) != 2:
+        raise ValueError("a PRNG key is an int or two 32-bit words")
+    return (words[0] << 32) | words[1]
+
+
+def apply_updates(params, updates, key=None, stochastic: bool = True):
+    """rollfast.utils.apply_updates (utils.py:648-708) on the
+    ``rf_apply_updates`` kernel: ``p + u`` in float32, cast to the parameter
+    dtype; bfloat16 parameters round stochastically when ``stochastic``
+    (utils.py:342-371).  Each leaf gets its own noise stream (the reference
+    splits ``key`` per leaf); the bits differ from JAX's Threefry stream, so
+    stochastic results agree with the reference in distribution only.
+    Returns new parameter tensors."""
+    if stochastic and key is None:
+        raise ValueError(
+            "apply_updates requires a PRNG `key` when stochastic=True. "
+            "Pass stochastic=False for deterministic rounding."
+        )
+    seed = key_seed(key) if stochastic else 0
+    leaves, treedef = tree_flatten(params, is_leaf=is_aux_leaf)
+    ups = tree_flatten(updates, is_leaf=is_aux_leaf)[0]
+    if len(ups) != len(leaves):
+        raise ValueError("params and updates must have the same tree structure")
+    items, outs = [], []
+    for idx, (p, u) in enumerate(zip(leaves, ups)):
+        if is_aux_leaf(p) or is_aux_leaf(u):
+            outs.append(p)
+            continue
+        require_cuda(p, "param")
+        require_cuda(u, "update")
+        if p.shape != u.shape:
+            raise ValueError(f"leaf {idx}: param shape {tuple(p.shape)} != update shape {tuple(u.shape)}")
+        out = torch.empty_like(p, memory_format=torch.contiguous_format)
+        items.append((p.contiguous(), u.contiguous(), out, _splitmix64(seed + idx) if stochastic else 0))
+        outs.append(out)
+    if items:
+        lib = _lib.load()
+        arr = (_lib.RfApplyLeaf * len(items))()
+        for i, (p, u, out, sd) in enumerate(items):
+            arr[i].param = p.data_ptr()
+            arr[i].update = u.data_ptr()
+            arr[i].out = out.data_ptr()
+            arr[i].n = p.numel()
+            arr[i].param_dtype = rf_dtype(p)
+            arr[i].update_dtype = rf_dtype(u)
+            arr[i].seed = sd
+        _lib.check(lib.rf_apply_updates(arr, len(items), int(bool(stochastic)),
+                                        torch.cuda.current_stream(items[0][0].device).cuda_stream))
+    return tree_unflatten(treedef, outs)

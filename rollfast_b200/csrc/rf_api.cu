@@ -674,6 +674,37 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
                       static_cast<cudaStream_t>(stream), nullptr);
 }
 
+rf_status rf_apply_updates(const rf_apply_leaf* leaves, int32_t n_leaves, int32_t stochastic, void* stream) {
+  if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
+    ApplyLaunch A{};
+    A.stochastic = stochastic ? 1 : 0;
+    int64_t chunks = 0;
+    for (int i = s; i < std::min(n_leaves, s + kMaxLeavesPerLaunch); ++i) {
+      const rf_apply_leaf& l = leaves[i];
+      const std::string where = "apply leaf " + std::to_string(i) + ": ";
+      if (l.n < 0 || (l.n > 0 && (!l.param || !l.update || !l.out))) return fail(RF_EINVAL, where + "bad pointers");
+      if (!valid_dtype(l.param_dtype) || !valid_dtype(l.update_dtype)) return fail(RF_EINVAL, where + "bad dtype");
+      ApplyLeafDev& d = A.leaf[A.n++];
+      d.p = l.param;
+      d.u = l.update;
+      d.out = l.out;
+      d.n = l.n;
+      d.chunk_begin = chunks;
+      d.pdt = l.param_dtype;
+      d.udt = l.update_dtype;
+      d.seed = l.seed;
+      d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.param) % 16 == 0) &&
+                 (reinterpret_cast<uintptr_t>(l.update) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.out) % 16 == 0);
+      chunks += ceil_div(l.n, kChunk);
+    }
+    A.total_chunks = chunks;
+    RF_TRY(launch_apply(A, st));
+  }
+  return RF_OK;
+}
+
 rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, int32_t max_ctas_per_sm,
                        void* stream) {
   if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");

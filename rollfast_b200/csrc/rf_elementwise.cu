@@ -501,6 +501,68 @@ __global__ void __launch_bounds__(kEwThreads) k_adaptive_finalize(const __grid_c
 }
 
 // ---------------------------------------------------------------------------
+// apply_updates (utils.py:648-708) with the bf16 stochastic rounding of
+// utils.py:342-371.  Noise: the SplitMix64 sequence (Steele, Lea and Flood,
+// "Fast splittable pseudorandom number generators", 2014), output c for the
+// elements 4c..4c+3, 16 bits each from the low end.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t c) {
+  uint64_t z = seed + (c + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// float32 -> the bfloat16 value (as a float) by adding 16 bits of noise
+// below the bf16 significand and truncating; +-Inf / NaN get no noise.
+__device__ __forceinline__ float sr_bf16(float x, uint32_t noise16) {
+  uint32_t b = __float_as_uint(x);
+  if ((b & 0x7FFFFFFFu) >= 0x7F800000u) noise16 = 0u;
+  return __uint_as_float((b + noise16) & 0xFFFF0000u);
+}
+
+__global__ void __launch_bounds__(kEwThreads) k_apply(const __grid_constant__ ApplyLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const ApplyLeafDev& L = P.leaf[find_leaf(s_begin, P.n, chunk)];
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    const bool sr = P.stochastic && L.pdt == RF_BF16;
+    if (L.vec_ok) {
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float p[8], u[8];
+        ld8(L.p, L.pdt, i, p);
+        ld8(L.u, L.udt, i, u);
+        uint64_t r0 = 0, r1 = 0;
+        if (sr) {
+          r0 = splitmix64_at(L.seed, uint64_t(i) >> 2);
+          r1 = splitmix64_at(L.seed, (uint64_t(i) >> 2) + 1);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float sum = __fadd_rn(p[k], u[k]);
+          // An SR result is exactly representable, so st8's conversion keeps it.
+          p[k] = sr ? sr_bf16(sum, uint32_t(((k < 4 ? r0 : r1) >> (16 * (k & 3))) & 0xFFFFu)) : sum;
+        }
+        st8(L.out, L.pdt, i, p);
+      }
+    } else {
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float sum = __fadd_rn(ld_as_float(L.p, L.pdt, i), ld_as_float(L.u, L.udt, i));
+        float v = sum;
+        if (sr) {
+          const uint64_t r = splitmix64_at(L.seed, uint64_t(i) >> 2);
+          v = sr_bf16(sum, uint32_t((r >> (16 * (i & 3))) & 0xFFFFu));
+        }
+        st_from_float(L.out, L.pdt, i, v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host launchers.
 // ---------------------------------------------------------------------------
 static int ew_grid(int64_t work, int ctas_per_sm = 8) {
@@ -565,6 +627,12 @@ rf_status launch_adaptive_finalize(const AdaptiveLaunch& P, float* ip, cudaStrea
   if (P.n == 0) return RF_OK;
   k_adaptive_finalize<<<P.n, kEwThreads, 0, st>>>(P, ip);
   return check_launch("k_adaptive_finalize");
+}
+
+rf_status launch_apply(const ApplyLaunch& P, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  k_apply<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  return check_launch("k_apply");
 }
 
 rf_status launch_tail(const TailLaunch& P, cudaStream_t st) {

@@ -194,6 +194,24 @@ struct AdaptiveLaunch {
   float* partials;  // [total_chunks]
 };
 rf_status launch_adaptive_dot(const AdaptiveLaunch& P, int gdt, cudaStream_t st);
+
+// apply_updates (utils.py:648-708).
+struct ApplyLeafDev {
+  const void* p;
+  const void* u;
+  void* out;
+  int64_t n, chunk_begin;
+  int32_t pdt, udt;
+  int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
+  uint64_t seed;
+};
+struct ApplyLaunch {
+  ApplyLeafDev leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  int stochastic;
+};
+rf_status launch_apply(const ApplyLaunch& P, cudaStream_t st);
 rf_status launch_adaptive_finalize(const AdaptiveLaunch& P, float* ip, cudaStream_t st);
 
 // Preconditioning variants (rf_precond.cu).  Reads A~ = sa X_F X_F^T of one

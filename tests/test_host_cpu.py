@@ -278,3 +278,19 @@ def test_tree_map_aux_leaf_semantics():
     out2 = tree_map(lambda x: "aux" if (x is None or isinstance(x, MaskedNode)) else "leaf", t,
                     is_leaf=lambda x: x is None or isinstance(x, MaskedNode))
     assert out2["b"] == "aux" and out2["c"] == "aux" and out2["a"] == "leaf"
+
+
+def test_apply_updates_requires_key_when_stochastic():
+    # utils.py:674-678
+    with pytest.raises(ValueError, match="requires a PRNG `key`"):
+        rf.apply_updates({"w": torch.ones(4)}, {"w": torch.ones(4)})
+
+
+def test_key_seed_layouts():
+    from rollfast_b200.base import key_seed
+
+    assert key_seed(torch.tensor([0, 42])) == 42
+    assert key_seed([1, 2]) == (1 << 32) | 2
+    assert key_seed(7) == 7
+    with pytest.raises(ValueError):
+        key_seed([1, 2, 3])

@@ -317,3 +317,45 @@ def test_aol_and_schatten_equal_rescaled_standard_iterations(shape):
             y = c[0] * y + B @ y
         want = np.swapaxes(y, -1, -2) if shape[-2] > shape[-1] else y
         np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
+
+
+# ---------------------------------------------------------------------------
+# apply_updates / bf16 stochastic rounding (utils.py:342-371, 648-708).
+# ---------------------------------------------------------------------------
+
+
+def test_splitmix64_published_first_outputs():
+    # SplitMix64 from state 0: the sequence's first two outputs.
+    assert int(O.splitmix64(np.uint64(0))) == 0xE220A8397B1DCDAF
+    assert int(O.splitmix64(np.uint64(0x9E3779B97F4A7C15))) == 0x6E789E6AA1B965F4
+    n = O.noise16(0, 5)
+    assert n.tolist() == [0xCDAF, 0x7B1D, 0xA839, 0xE220, 0x65F4]
+
+
+def test_stochastic_round_bf16_known_answers():
+    f = np.float32
+    # exactly representable values never move, whatever the noise
+    for x in (1.0, -2.5, 0.0, 2.0 ** 127):
+        for nz in (0, 0x7FFF, 0xFFFF):
+            assert O.stochastic_round_bf16(np.array([x], f), np.array([nz]))[0] == f(x)
+    # halfway between 1 and 1 + 2^-7: rounds up exactly when noise >= 0x8000
+    half = np.array([1.0 + 2.0 ** -8], f)
+    assert O.stochastic_round_bf16(half, np.array([0x7FFF]))[0] == 1.0
+    assert O.stochastic_round_bf16(half, np.array([0x8000]))[0] == f(1.0 + 2.0 ** -7)
+    # utils.py:344-346: +-Inf with the largest noise stays +-Inf; NaN stays NaN
+    inf = O.stochastic_round_bf16(np.array([np.inf, -np.inf, np.nan], f), np.array([0xFFFF] * 3))
+    assert inf[0] == np.inf and inf[1] == -np.inf and np.isnan(inf[2])
+
+
+def test_apply_updates_deterministic_and_unbiased():
+    rng = np.random.default_rng(0)
+    p = O.bf16_round(np.ones(200000, np.float32))
+    u = np.full(200000, 1e-3, np.float32)  # below half a bf16 ulp at 1.0 (2^-8)
+    det = O.apply_updates(p, u, "bfloat16", stochastic=False)
+    assert np.all(det == 1.0)  # round-to-nearest loses the update (utils.py:653-656)
+    sr = O.apply_updates(p, u, "bfloat16", stochastic=True, seed=int(rng.integers(1 << 62)))
+    assert set(np.unique(sr).tolist()) <= {1.0, 1.0078125}
+    assert abs(float(sr.mean()) - 1.001) < 2e-5  # E[SR(x)] = x
+    x = rng.standard_normal(1000).astype(np.float32)
+    assert np.array_equal(O.apply_updates(x, x, "float32"), x + x)
+    assert np.array_equal(O.apply_updates(x, x, "float16"), O.f16_round(x + x))
