@@ -260,6 +260,7 @@ def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
         upd, state = tx.update(dev_g, state, params)
         for hu, du in zip(leaves_of(host_u), leaves_of(upd)):
             hu.copy_(du, non_blocking=True)
+        upd = None  # the copies are stream-ordered before any reuse of these blocks
     e1.record()
     barrier()
     e_ms = e0.elapsed_time(e1) / k
@@ -330,7 +331,11 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    # Like a training loop, each step's updates are dropped (applied) before
+    # the next step: holding two update trees (2 x 30 GiB) beside the state
+    # and two gradient sets would leave little of the 178 GiB free.
     for i in range(args.warmup):
+        upd = None
         upd, state = tx.update(grad_sets[i % 2], state, params)
     barrier()
 
@@ -341,6 +346,7 @@ def main():
         barrier()
         start.record()
         for i in range(args.steps):
+            upd = None
             upd, state = tx.update(grad_sets[i % 2], state, params)
         stop.record()
         barrier()

@@ -60,7 +60,7 @@ typedef enum rf_ns_precision { RF_NS_F16 = 0, RF_NS_BF16 = 1, RF_NS_F32 = 2 } rf
  * rows > cols (orthogonalization.py:228-231). */
 typedef struct rf_muon_leaf {
   const void* grad;   /* [batch][rows][cols], grad_dtype */
-  float* mu;          /* [batch][rows][cols] fp32 momentum, updated in place */
+  float* mu;          /* [batch][rows][cols] momentum (mu_dtype storage), updated in place */
   const void* param;  /* [batch][rows][cols], param_dtype; may be NULL when decay == 0 */
   void* out;          /* [batch][rows][cols], out_dtype: the update (or O when the tail is deferred) */
   int64_t batch, rows, cols;
@@ -68,6 +68,14 @@ typedef struct rf_muon_leaf {
   float shape_scale;  /* muon.py:79-100 factor for this leaf */
   float decay;        /* weight decay for this leaf (0 when masked out) */
   int32_t skip_ns;    /* 1: this rank does not own the leaf (multi-GPU); momentum/NS skipped */
+  /* RF_F32, or RF_BF16: momentum stored as bfloat16 (mu_dtype, muon.py:207-210).
+   * The step then reads the bf16 state, forms the new momentum and the
+   * direction in float32, and stores the new momentum stochastically rounded
+   * (utils.py:342-371, 412-425) with SplitMix64 noise from sr_seed; the
+   * reference draws JAX Threefry bits, so the stored state agrees with it in
+   * distribution, not bit for bit. */
+  int32_t mu_dtype;
+  uint64_t sr_seed;
 } rf_muon_leaf;
 
 /* Newton-Schulz preconditioning (orthogonalization.py:24, 153-176, 233-250). */
@@ -173,8 +181,8 @@ rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, i
 /* (N)AdamW fallback leaves (adam.py:123-233 + decay + LR). */
 typedef struct rf_adam_leaf {
   const void* grad;   /* [n], grad_dtype */
-  float* mu;          /* [n] fp32, in place */
-  float* nu;          /* [n] fp32, in place */
+  float* mu;          /* [n] first moment (state_dtype storage), in place */
+  float* nu;          /* [n] second moment (state_dtype storage), in place */
   const void* param;  /* [n], param_dtype; may be NULL when decay == 0 */
   void* out;          /* [n], out_dtype */
   int64_t n;
@@ -184,6 +192,10 @@ typedef struct rf_adam_leaf {
    * optax.add_decayed_weights (weakly typed Python float), RF_F32 for the
    * in-transform decay of scale_by_adam (utils.py:79-90). */
   int32_t decay_rounding;
+  /* RF_F32, or RF_BF16: both moments stored as bfloat16 with stochastic
+   * rounding (adam.py:219-222), noise streams from the two seeds. */
+  int32_t state_dtype;
+  uint64_t sr_seed_mu, sr_seed_nu;
 } rf_adam_leaf;
 typedef struct rf_adam_params {
   /* b1, b2 as the caller's double-precision scalars: the reference forms

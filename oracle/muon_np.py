@@ -24,6 +24,7 @@ import numpy as np
 __all__ = [
     "PRECONDITIONINGS",
     "apply_updates",
+    "store_state",
     "noise16",
     "splitmix64",
     "stochastic_round_bf16",
@@ -520,6 +521,16 @@ def momentum_runtime(g: np.ndarray, mu: np.ndarray, count: int, beta: float, *, 
         g_t = gf
     d = (b * mu_t + s * g_t) if nesterov else mu_t
     return mu_new, d.astype(dtype)
+
+
+def store_state(x: np.ndarray, state_dtype: str, seed: int = 0) -> np.ndarray:
+    """utils.py:412-425 / adam.py:219-225: the stored optimizer state.
+    float32 is kept as is; bfloat16 rounds stochastically (utils.py:342-371)
+    with the library's noise16 stream of ``seed`` over the flat index."""
+    x = np.asarray(x, np.float32)
+    if state_dtype == "bfloat16":
+        return stochastic_round_bf16(x.reshape(-1), noise16(seed, x.size)).reshape(x.shape)
+    return x
 
 
 def shape_scale_factor(shape, dim_nums: MatrixDimensionNumbers, consistent_rms=None) -> np.float32:

@@ -84,6 +84,8 @@ class RfMuonLeaf(ctypes.Structure):
         ("shape_scale", ctypes.c_float),
         ("decay", ctypes.c_float),
         ("skip_ns", ctypes.c_int32),
+        ("mu_dtype", ctypes.c_int32),
+        ("sr_seed", ctypes.c_uint64),
     ]
 
 
@@ -134,6 +136,9 @@ class RfAdamLeaf(ctypes.Structure):
         ("out_dtype", ctypes.c_int32),
         ("decay", ctypes.c_float),
         ("decay_rounding", ctypes.c_int32),
+        ("state_dtype", ctypes.c_int32),
+        ("sr_seed_mu", ctypes.c_uint64),
+        ("sr_seed_nu", ctypes.c_uint64),
     ]
 
 

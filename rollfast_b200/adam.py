@@ -23,6 +23,8 @@ from .base import (
     resolve_scalar,
     round_to_dtype,
     safe_increment,
+    sr_step_seeds,
+    state_dtype,
 )
 from .tree import MaskedNode, is_aux_leaf, tree_flatten, tree_unflatten
 
@@ -53,16 +55,10 @@ def zeros_like_tree(params, dtype=torch.float32):
     )
 
 
-def _check_mu_dtype(mu_dtype) -> None:
-    if mu_dtype is not None and mu_dtype not in (torch.float32, "float32", "f32"):
-        raise NotImplementedError(
-            "mu_dtype other than float32 (stochastically rounded bf16 state) is not on the B200 hot path"
-        )
-
-
 def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float,
-             max_ctas_per_sm: int = 0) -> None:
-    """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype)."""
+             max_ctas_per_sm: int = 0, seeds=None) -> None:
+    """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype);
+    ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state."""
     if not items:
         return
     lib = _lib.load()
@@ -79,6 +75,9 @@ def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: fl
         arr[i].out_dtype = rf_dtype(out)
         arr[i].decay = decay
         arr[i].decay_rounding = rdt
+        arr[i].state_dtype = rf_dtype(mu)
+        if seeds is not None:
+            arr[i].sr_seed_mu, arr[i].sr_seed_nu = seeds[2 * i], seeds[2 * i + 1]
     prm = _lib.RfAdamParams(float(b1), float(b2), float(eps), float(eps_root), int(count), int(bool(nesterov)),
                             float(lr), int(max_ctas_per_sm))
     _lib.check(lib.rf_adamw_update(arr, len(items), prm,
@@ -114,6 +113,15 @@ def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_round
     return items, outs, treedef
 
 
+def adam_seeds(items, key):
+    """(seeds, next key) for the items' bfloat16 moments: two streams per
+    leaf (adam.py:219-222 splits its rounding key into one per moment); no
+    randomness and an unchanged key for float32 state."""
+    if not any(it[1].dtype == torch.bfloat16 for it in items):
+        return None, key
+    return sr_step_seeds(key, 2 * len(items))
+
+
 def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, weight_decay=0.0,
                   weight_decay_mask=None, nesterov: bool = False, use_magma: bool = False, magma_p: float = 0.5,
                   magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
@@ -122,12 +130,14 @@ def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, we
     decay when ``params`` are given (adam.py:185-201)."""
     if use_magma:
         raise NotImplementedError("Magma masking is not on the B200 hot path")
-    _check_mu_dtype(mu_dtype)
+    sdt = state_dtype(mu_dtype)
     if callable(weight_decay):
         raise NotImplementedError("scheduled weight_decay is not supported")
 
     def init_fn(params):
-        return ScaleByAdamState(new_count(0), zeros_like_tree(params), zeros_like_tree(params), (), fresh_key(key))
+        # adam.py:98-112: both moments in mu_dtype (float32 by default).
+        return ScaleByAdamState(new_count(0), zeros_like_tree(params, sdt), zeros_like_tree(params, sdt), (),
+                                fresh_key(key))
 
     def update_fn(updates, state, params=None):
         if has_nonzero_or_scheduled(weight_decay) and params is None:
@@ -139,8 +149,10 @@ def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, we
         mask = resolve_mask(weight_decay_mask, params) if params is not None else None
         items, outs, treedef = _adam_items(updates, state, params, decay=float(weight_decay), decay_mask=mask,
                                            decay_rounding_param=False)
-        run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=count, nesterov=nesterov, lr=-1.0)
-        new_state = ScaleByAdamState(safe_increment(state.count), state.mu, state.nu, state.magma_s, state.key)
+        seeds, key_next = adam_seeds(items, state.key)
+        run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=count, nesterov=nesterov, lr=-1.0,
+                 seeds=seeds)
+        new_state = ScaleByAdamState(safe_increment(state.count), state.mu, state.nu, state.magma_s, key_next)
         return tree_unflatten(treedef, outs), new_state
 
     return GradientTransformation(init_fn, update_fn)
@@ -155,7 +167,7 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
     decay_on = has_nonzero_or_scheduled(weight_decay)
     if use_magma:
         raise NotImplementedError("Magma masking is not on the B200 hot path")
-    _check_mu_dtype(mu_dtype)
+    state_dtype(mu_dtype)  # validates
     if callable(weight_decay):
         raise NotImplementedError("scheduled weight_decay is not supported")
     inner = scale_by_adam(b1, b2, eps, eps_root, mu_dtype, nesterov=nesterov, key=key)
@@ -182,10 +194,11 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
         items, outs, treedef = _adam_items(updates, adam_state, params,
                                            decay=float(weight_decay) if decay_on else 0.0, decay_mask=mask,
                                            decay_rounding_param=True)
+        seeds, key_next = adam_seeds(items, adam_state.key)
         run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=host_count(adam_state.count),
-                 nesterov=nesterov, lr=lr)
+                 nesterov=nesterov, lr=lr, seeds=seeds)
         new_adam = ScaleByAdamState(safe_increment(adam_state.count), adam_state.mu, adam_state.nu,
-                                    adam_state.magma_s, adam_state.key)
+                                    adam_state.magma_s, key_next)
         new_lr = ScaleByScheduleState(safe_increment(lr_state.count)) if callable(learning_rate) else lr_state
         return tree_unflatten(treedef, outs), (new_adam, *state[1:-1], new_lr)
 

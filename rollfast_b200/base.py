@@ -341,6 +341,28 @@ def key_seed(key) -> int:
     return (words[0] << 32) | words[1]
 
 
+def state_dtype(mu_dtype) -> torch.dtype:
+    """Optimizer-state dtype for ``mu_dtype`` (muon.py:207-210, adam.py:98-106):
+    float32 by default; bfloat16 state is stored with stochastic rounding."""
+    if mu_dtype is None or mu_dtype in (torch.float32, "float32", "f32"):
+        return torch.float32
+    if mu_dtype in (torch.bfloat16, "bfloat16", "bf16"):
+        return torch.bfloat16
+    raise NotImplementedError(f"mu_dtype={mu_dtype!r}: float32 or bfloat16 optimizer state is supported")
+
+
+def sr_step_seeds(key, n: int) -> tuple[list, torch.Tensor]:
+    """Noise seeds for one step's stochastically rounded state (``n`` streams)
+    and the advanced key.  The reference splits its PRNG key once per step
+    (utils.py:545-562, adam.py:128-131) and draws Threefry bits; here the
+    key's 64 bits seed SplitMix64 streams instead."""
+    k = key_seed(key)
+    step = _splitmix64(k ^ 0xD1B54A32D192ED03)
+    seeds = [_splitmix64((step + i) & ((1 << 64) - 1)) for i in range(n)]
+    nk = _splitmix64(k)
+    return seeds, torch.tensor([(nk >> 32) & 0xFFFFFFFF, nk & 0xFFFFFFFF], dtype=torch.int64)
+
+
 def apply_updates(params, updates, key=None, stochastic: bool = True):
     """rollfast.utils.apply_updates (utils.py:648-708) on the
     ``rf_apply_updates`` kernel: ``p + u`` in float32, cast to the parameter

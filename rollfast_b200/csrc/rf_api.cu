@@ -97,6 +97,8 @@ struct LeafPlan {
   int gdt, pdt, odt;
   float shape_scale, decay;
   int64_t scale_index;  // first matrix in the scale array
+  int mu_bf16;          // momentum stored as bfloat16 (stochastic rounding)
+  uint64_t sr_seed;
 };
 
 struct GroupPlan {
@@ -179,6 +181,8 @@ static rf_status validate_leaf(const rf_muon_leaf& l, int i, bool need_out) {
   if (need_out && !l.out) return fail(RF_EINVAL, where + "out must be non-null");
   if (l.decay != 0.f && (!l.param || !valid_dtype(l.param_dtype)))
     return fail(RF_EINVAL, where + "param (valid dtype) required when decay != 0");
+  if (l.mu_dtype != RF_F32 && l.mu_dtype != RF_BF16)
+    return fail(RF_EINVAL, where + "mu_dtype must be float32 or bfloat16");
   return RF_OK;
 }
 
@@ -202,6 +206,7 @@ static rf_status prepare_norms(const Plan& P, const std::vector<int>& ids, const
         MomentumLeaf& ml = L.leaf[L.n++];
         ml.g = lp.g;
         ml.mu = lp.mu;
+        ml.mu_bf16 = lp.mu_bf16;
         ml.numel = lp.rows * lp.cols;
         ml.chunk_begin = chunks;
         ml.mat_begin = mats;
@@ -245,8 +250,8 @@ struct EventPool {
 // on `st`.  With `aux`, sub-batch k+1's preparation overlaps sub-batch k's
 // GEMMs; workspace regions alternate, so preparing k+2 waits for k's GEMMs.
 static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
-                              int ns_steps, float eps, int precond, int fuse_tail, float lr, int reserve_sms,
-                              void* ws, size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
+                              int ns_steps, float eps, int precond, int adaptive, int fuse_tail, float lr,
+                              int reserve_sms, void* ws, size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
   if (P.leaves.empty()) return RF_OK;
   if (!ws || ws_bytes < P.bytes)
     return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
@@ -314,6 +319,11 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       for (int li : sub) {
         const LeafPlan& lp = P.leaves[li];
         LoadLeaf& l = ld.leaf[ld.n++];
+        l.mu_bf16 = lp.mu_bf16;
+        l.sr_seed = lp.sr_seed;
+        // The last operand load stores a bf16 momentum, unless the adaptive
+        // pass (which still needs the previous state) runs afterwards.
+        l.store_mu = lp.mu_bf16 && !adaptive && precond == RF_PRECOND_FROBENIUS;
         l.g = lp.g;
         l.mu = lp.mu;
         l.rows = lp.rows;
@@ -373,6 +383,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         RF_TRY(launch_precondition(precond, P.precision, Am, G, gp.m, gp.mp, sc.sa, begins, nidx, ld.n, denom, eps,
                                    Bm, abytes, X1, xbytes, &rows, st));
         ld.row_scale = rows;
+        for (int i = 0; i < ld.n; ++i) ld.leaf[i].store_mu = ld.leaf[i].mu_bf16 && !adaptive;
         for (int gdt : {int(RF_F32), int(RF_BF16), int(RF_F16)}) {
           bool any = false;
           for (int li : sub) any |= P.leaves[li].gdt == gdt;
@@ -447,6 +458,8 @@ static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vec
     p.odt = l.out_dtype;
     p.shape_scale = l.shape_scale;
     p.decay = l.decay;
+    p.mu_bf16 = l.mu_dtype == RF_BF16;
+    p.sr_seed = l.sr_seed;
     out.push_back(p);
   }
   return RF_OK;
@@ -522,6 +535,8 @@ static rf_status adaptive_pass(const Plan& P, const MomentumCoeffs& mc, int fuse
       AdaptiveLeaf& a = A.leaf[A.n++];
       a.g = lp.g;
       a.mu = lp.mu;
+      a.mu_bf16 = lp.mu_bf16;
+      a.sr_seed = lp.sr_seed;
       a.o = lp.out;
       a.n = n;
       a.chunk_begin = chunks;
@@ -575,12 +590,12 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
     return fail(RF_EINVAL, "unknown preconditioning");
   if (p.adaptive) {
     const MomentumCoeffs mc = momentum_coeffs(p);
-    RF_TRY(run_pipeline(P, mc, p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 0, 0.f, p.reserve_sms,
+    RF_TRY(run_pipeline(P, mc, p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 1, 0, 0.f, p.reserve_sms,
                         workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                         static_cast<cudaStream_t>(p.aux_stream)));
     return adaptive_pass(P, mc, p.fuse_tail, p.lr, workspace, static_cast<cudaStream_t>(stream));
   }
-  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning,
+  return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 0,
                       p.fuse_tail, p.lr,
                       p.reserve_sms, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                       static_cast<cudaStream_t>(p.aux_stream));
@@ -611,6 +626,8 @@ rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const 
     d.n = l.batch * l.rows * l.cols;
     d.chunk_begin = chunks;
     d.gdt = l.grad_dtype;
+    d.mu_bf16 = l.mu_dtype == RF_BF16;
+    d.sr_seed = l.sr_seed;
     chunks += ceil_div(d.n, kChunk);
     if (D.n == kMaxLeavesPerLaunch) {
       D.total_chunks = chunks;
@@ -670,7 +687,7 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
   RF_TRY(ns_plan(batch, rows, cols, precision, P, x, x_dtype, out, out_dtype));
   MomentumCoeffs mc{};
   mc.mode = kDirIdentity;
-  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, preconditioning, 0, 0.f, 0, workspace, workspace_bytes,
+  return run_pipeline(P, mc, coeffs, n_coeff_rows, iters, eps, preconditioning, 0, 0, 0.f, 0, workspace, workspace_bytes,
                       static_cast<cudaStream_t>(stream), nullptr);
 }
 
@@ -791,6 +808,11 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
       d.odt = l.out_dtype;
       d.decay = l.decay;
       d.decay_dt = l.decay_rounding;
+      if (l.state_dtype != RF_F32 && l.state_dtype != RF_BF16)
+        return fail(RF_EINVAL, "adam leaf: state_dtype must be float32 or bfloat16");
+      d.sdt = l.state_dtype;
+      d.seed_mu = l.sr_seed_mu;
+      d.seed_nu = l.sr_seed_nu;
       d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.nu) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&

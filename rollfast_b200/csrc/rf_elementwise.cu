@@ -122,6 +122,54 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // ---------------------------------------------------------------------------
+// Stochastic rounding to bfloat16 (utils.py:342-371): 16 bits of noise added
+// below the bf16 significand, then truncation; +-Inf / NaN get no noise.
+// The noise is the SplitMix64 sequence (Steele, Lea and Flood, "Fast
+// splittable pseudorandom number generators", 2014) of a per-leaf seed:
+// output c serves elements 4c..4c+3, 16 bits each from the low end.  Used for
+// bfloat16 optimizer state (utils.py:412-425, adam.py:219-222) and
+// apply_updates.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t c) {
+  uint64_t z = seed + (c + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float sr_bf16(float x, uint32_t noise16) {
+  uint32_t b = __float_as_uint(x);
+  if ((b & 0x7FFFFFFFu) >= 0x7F800000u) noise16 = 0u;
+  return __uint_as_float((b + noise16) & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ uint32_t sr_noise(uint64_t seed, int64_t i) {
+  return uint32_t((splitmix64_at(seed, uint64_t(i) >> 2) >> (16 * (i & 3))) & 0xFFFFu);
+}
+
+// v[0..7] -> bf16 at p[i..i+7] (i % 8 == 0, 16-byte aligned), stochastically rounded.
+__device__ __forceinline__ void sr_store8_bf16(void* p, int64_t i, const float* v, uint64_t seed) {
+  const uint64_t r0 = splitmix64_at(seed, uint64_t(i) >> 2), r1 = splitmix64_at(seed, (uint64_t(i) >> 2) + 1);
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = __float_as_uint(sr_bf16(v[2 * k], uint32_t(((k < 2 ? r0 : r1) >> (32 * (k & 1))) & 0xFFFFu)));
+    const uint32_t hi =
+        __float_as_uint(sr_bf16(v[2 * k + 1], uint32_t(((k < 2 ? r0 : r1) >> (32 * (k & 1) + 16)) & 0xFFFFu)));
+    w[k] = (lo >> 16) | (hi & 0xFFFF0000u);
+  }
+  *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void sr_store1_bf16(void* p, int64_t i, float v, uint64_t seed) {
+  static_cast<uint16_t*>(p)[i] = uint16_t(__float_as_uint(sr_bf16(v, sr_noise(seed, i))) >> 16);
+}
+
+__device__ __forceinline__ float ld_bf16(const void* p, int64_t i) {
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+// ---------------------------------------------------------------------------
 // k_momentum_sumsq: one CTA per chunk of kChunk elements of one matrix.
 // ---------------------------------------------------------------------------
 template <int GDT>
@@ -140,7 +188,21 @@ __global__ void __launch_bounds__(kEwThreads) k_momentum_sumsq(const __grid_cons
     const int64_t lo = cim * kChunk;
     const int64_t hi = (lo + kChunk < L.numel ? lo + kChunk : L.numel);
     float acc = 0.f;
-    if (L.vec_ok) {
+    if (L.vec_ok && L.mu_bf16) {
+      // bfloat16 state: the new momentum only feeds the norm here; the
+      // operand load recomputes it and stores it (stochastically rounded).
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float g[8], m[8];
+        GradVec<GDT>::load8(L.g, base + i, g);
+        GradVec<RF_BF16>::load8(L.mu, base + i, m);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          m[k] = momentum_new(P.c, g[k], m[k]);
+          const float d = direction(P.c, g[k], m[k]);
+          acc = fmaf(d, d, acc);
+        }
+      }
+    } else if (L.vec_ok) {
       for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
         float g[8], m[8];
         GradVec<GDT>::load8(L.g, base + i, g);
@@ -160,10 +222,10 @@ __global__ void __launch_bounds__(kEwThreads) k_momentum_sumsq(const __grid_cons
     } else {
       for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float g = ld_as_float(L.g, GDT, base + i);
-        float m = L.mu ? L.mu[base + i] : 0.f;
+        float m = L.mu ? (L.mu_bf16 ? ld_bf16(L.mu, base + i) : L.mu[base + i]) : 0.f;
         if (L.mu) {
           m = momentum_new(P.c, g, m);
-          L.mu[base + i] = m;
+          if (!L.mu_bf16) L.mu[base + i] = m;
         }
         const float d = direction(P.c, g, m);
         acc = fmaf(d, d, acc);
@@ -248,7 +310,12 @@ __device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int
     const int64_t idx = base + ir * L.cols + ic;
     float g[8], m[8];
     load8_any<GDT>(L.g, idx, g);
-    if (L.mu) {
+    if (L.mu && L.mu_bf16) {
+      GradVec<RF_BF16>::load8(L.mu, idx, m);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[k] = momentum_new(P.c, g[k], m[k]);
+      if (L.store_mu) sr_store8_bf16(const_cast<float*>(L.mu), idx, m, L.sr_seed);
+    } else if (L.mu) {
       const float4* mp = reinterpret_cast<const float4*>(L.mu + idx);
       const float4 a = mp[0], b = mp[1];
       m[0] = a.x; m[1] = a.y; m[2] = a.z; m[3] = a.w; m[4] = b.x; m[5] = b.y; m[6] = b.z; m[7] = b.w;
@@ -266,7 +333,13 @@ __device__ __forceinline__ void dir8(const LoadLaunch& P, const LoadLeaf& L, int
       if (ir < L.rows && c < L.cols) {
         const int64_t idx = base + ir * L.cols + c;
         const float g = ld_as_float(L.g, GDT, idx);
-        const float m = L.mu ? L.mu[idx] : 0.f;
+        float m = 0.f;
+        if (L.mu && L.mu_bf16) {
+          m = momentum_new(P.c, g, ld_bf16(L.mu, idx));
+          if (L.store_mu) sr_store1_bf16(const_cast<float*>(L.mu), idx, m, L.sr_seed);
+        } else if (L.mu) {
+          m = L.mu[idx];
+        }
         x = direction_fast(P.c, g, m) * scale;
       }
       v[k] = x;
@@ -383,23 +456,33 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
       for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
         float g[8], mu[8], nu[8], p[8], u[8];
         ld8(L.g, L.gdt, i, g);
-        ld8(L.mu, RF_F32, i, mu);
-        ld8(L.nu, RF_F32, i, nu);
+        ld8(L.mu, L.sdt, i, mu);
+        ld8(L.nu, L.sdt, i, nu);
         if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
 #pragma unroll
         for (int k = 0; k < 8; ++k) u[k] = adam_one(c, L, g[k], mu[k], nu[k], L.decay != 0.f ? p[k] : 0.f);
-        st8(L.mu, RF_F32, i, mu);
-        st8(L.nu, RF_F32, i, nu);
+        if (L.sdt == RF_BF16) {  // adam.py:219-222: both moments stochastically rounded
+          sr_store8_bf16(L.mu, i, mu, L.seed_mu);
+          sr_store8_bf16(L.nu, i, nu, L.seed_nu);
+        } else {
+          st8(L.mu, RF_F32, i, mu);
+          st8(L.nu, RF_F32, i, nu);
+        }
         st8(L.out, L.odt, i, u);
       }
     } else {
       for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float g = ld_as_float(L.g, L.gdt, i);
-        float mu = L.mu[i], nu = L.nu[i];
+        float mu = ld_as_float(L.mu, L.sdt, i), nu = ld_as_float(L.nu, L.sdt, i);
         const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
         const float u = adam_one(c, L, g, mu, nu, p);
-        L.mu[i] = mu;
-        L.nu[i] = nu;
+        if (L.sdt == RF_BF16) {
+          sr_store1_bf16(L.mu, i, mu, L.seed_mu);
+          sr_store1_bf16(L.nu, i, nu, L.seed_nu);
+        } else {
+          static_cast<float*>(L.mu)[i] = mu;
+          static_cast<float*>(L.nu)[i] = nu;
+        }
         st_from_float(L.out, L.odt, i, u);
       }
     }
@@ -420,8 +503,9 @@ __global__ void __launch_bounds__(kEwThreads) k_direction(const __grid_constant_
     const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
     for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
       const float g = ld_as_float(L.g, L.gdt, i);
-      const float m = momentum_new(P.c, g, L.mu[i]);
-      L.mu[i] = m;
+      const float m = momentum_new(P.c, g, L.mu_bf16 ? ld_bf16(L.mu, i) : L.mu[i]);
+      if (L.mu_bf16) sr_store1_bf16(L.mu, i, m, L.sr_seed);
+      else L.mu[i] = m;
       L.out[i] = direction(P.c, g, m);
     }
   }
@@ -482,8 +566,17 @@ __global__ void __launch_bounds__(kEwThreads) k_adaptive_dot(const __grid_consta
     const int64_t lo = (chunk - L.chunk_begin) * kChunk;
     const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
     float s = 0.f;
-    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
-      s += direction(P.c, ld_as_float(L.g, GDT, i), L.mu[i]) * ld_as_float(L.o, L.odt, i);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const float g = ld_as_float(L.g, GDT, i);
+      float m;
+      if (L.mu_bf16) {  // previous bf16 state: recompute, and store it here
+        m = momentum_new(P.c, g, ld_bf16(L.mu, i));
+        sr_store1_bf16(L.mu, i, m, L.sr_seed);
+      } else {
+        m = L.mu[i];
+      }
+      s += direction(P.c, g, m) * ld_as_float(L.o, L.odt, i);
+    }
     s = block_sum(s, red);
     if (threadIdx.x == 0) P.partials[chunk] = s;
   }
@@ -502,25 +595,8 @@ __global__ void __launch_bounds__(kEwThreads) k_adaptive_finalize(const __grid_c
 
 // ---------------------------------------------------------------------------
 // apply_updates (utils.py:648-708) with the bf16 stochastic rounding of
-// utils.py:342-371.  Noise: the SplitMix64 sequence (Steele, Lea and Flood,
-// "Fast splittable pseudorandom number generators", 2014), output c for the
-// elements 4c..4c+3, 16 bits each from the low end.
+// utils.py:342-371 (helpers at the top of this file).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t c) {
-  uint64_t z = seed + (c + 1) * 0x9E3779B97F4A7C15ull;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-// float32 -> the bfloat16 value (as a float) by adding 16 bits of noise
-// below the bf16 significand and truncating; +-Inf / NaN get no noise.
-__device__ __forceinline__ float sr_bf16(float x, uint32_t noise16) {
-  uint32_t b = __float_as_uint(x);
-  if ((b & 0x7FFFFFFFu) >= 0x7F800000u) noise16 = 0u;
-  return __uint_as_float((b + noise16) & 0xFFFF0000u);
-}
-
 __global__ void __launch_bounds__(kEwThreads) k_apply(const __grid_constant__ ApplyLaunch P) {
   __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
   for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;

@@ -38,6 +38,7 @@ struct MomentumLeaf {
   int64_t scale_index;   // index of its first matrix in the per-matrix scale array
   int32_t chunks_per_mat;
   int32_t vec_ok;        // 16-byte aligned and numel % 8 == 0
+  int32_t mu_bf16;       // mu stored as bfloat16: read it, leave the store to the operand load
 };
 
 struct MomentumLaunch {
@@ -58,6 +59,10 @@ struct LoadLeaf {
   int32_t transposed;
   int32_t gdt;               // grad dtype; a launch handles the leaves of one dtype
   int32_t vec_ok;            // cols % 8 == 0 and 16-byte aligned grad / mu
+  // bfloat16 momentum: mu holds the previous state; this load recomputes the
+  // new momentum and, with store_mu, writes it back stochastically rounded.
+  int32_t mu_bf16, store_mu;
+  uint64_t sr_seed;
 };
 
 struct LoadLaunch {
@@ -81,14 +86,16 @@ struct AdamCoeffs {
 };
 struct AdamLeafDev {
   const void* g;
-  float* mu;
-  float* nu;
+  void* mu;
+  void* nu;
   const void* p;
   void* out;
   int64_t n, chunk_begin;
   int32_t gdt, pdt, odt, decay_dt;
   int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
   float decay;
+  int32_t sdt;     // moment storage dtype: RF_F32, or RF_BF16 (stochastic rounding)
+  uint64_t seed_mu, seed_nu;
 };
 struct AdamLaunch {
   AdamLeafDev leaf[kMaxLeavesPerLaunch];
@@ -100,10 +107,12 @@ struct AdamLaunch {
 
 struct DirLeafDev {
   const void* g;
-  float* mu;
+  float* mu;  // bfloat16 storage when mu_bf16
   float* out;
   int64_t n, chunk_begin;
   int32_t gdt;
+  int32_t mu_bf16;
+  uint64_t sr_seed;
 };
 struct DirLaunch {
   DirLeafDev leaf[kMaxLeavesPerLaunch];
@@ -181,10 +190,12 @@ rf_status launch_tail(const TailLaunch& P, cudaStream_t st);
 // Nesterov / bias-corrected direction recomputed from g and the updated mu.
 struct AdaptiveLeaf {
   const void* g;
-  const float* mu;
+  float* mu;  // updated momentum; with mu_bf16 the previous bf16 state, stored here
   const void* o;
   int64_t n, chunk_begin;
   int32_t gdt, odt;
+  int32_t mu_bf16;
+  uint64_t sr_seed;
 };
 struct AdaptiveLaunch {
   AdaptiveLeaf leaf[kMaxLeavesPerLaunch];

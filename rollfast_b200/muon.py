@@ -20,7 +20,7 @@ from typing import Any, NamedTuple
 import torch
 
 from . import _lib, _runtime
-from .adam import ScaleByAdamState, adamw, fresh_key, run_adam, zeros_like_tree
+from .adam import ScaleByAdamState, adam_seeds, adamw, fresh_key, run_adam, zeros_like_tree
 from .base import (
     AddDecayedWeightsState,
     EmptyState,
@@ -45,6 +45,8 @@ from .base import (
     run_tail,
     safe_increment,
     scale_by_learning_rate,
+    sr_step_seeds,
+    state_dtype,
     stream_handle,
     validate_beta,
     validate_positive,
@@ -128,6 +130,7 @@ class _MuonLeaf(NamedTuple):
     layout: Any
     shape: tuple
     spec: MatrixDimensionNumbers
+    seed: int = 0         # noise seed of a bfloat16 momentum store
 
 
 def _as_matrix(t: torch.Tensor, lay) -> torch.Tensor:
@@ -178,7 +181,19 @@ def _leaf_table(ml: list, scales, decays):
         e.shape_scale = scales[i]
         e.decay = decays[i]
         e.skip_ns = 0
+        e.mu_dtype = rf_dtype(L.mu)
+        e.sr_seed = L.seed
     return arr
+
+
+def _seed_leaves(ml: list, key):
+    """Per-leaf noise seeds for bfloat16 momentum (utils.py:545-562 splits the
+    state key when it rounds stochastically) and the state's next key; float32
+    momentum consumes no randomness and keeps the key."""
+    if not any(L.mu.dtype == torch.bfloat16 for L in ml):
+        return ml, key
+    seeds, key_next = sr_step_seeds(key, len(ml))
+    return [L._replace(seed=sd) for L, sd in zip(ml, seeds)], key_next
 
 
 def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail, reserve_sms=0,
@@ -279,8 +294,7 @@ def _check_supported(*, adaptive, preconditioning, use_magma, mu_dtype, orthogon
     if adaptive and orthogonalize_fn is not orthogonalize_via_newton_schulz:
         raise NotImplementedError("adaptive=True with a custom orthogonalize_fn is not supported "
                                   "(the default Newton-Schulz path computes <mu_hat, O> on the GPU)")
-    if mu_dtype is not None and mu_dtype not in (torch.float32, "float32", "f32"):
-        raise NotImplementedError("mu_dtype other than float32 (stochastic-rounding bf16 state) is not supported")
+    state_dtype(mu_dtype)  # float32, or bfloat16 with stochastic rounding
     if preconditioning not in ("frobenius", "spectral", "aol", "schatten"):
         raise ValueError(f"Unknown preconditioning {preconditioning!r}.")
 
@@ -309,8 +323,9 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
                      orthogonalize_fn=orthogonalize_fn)
 
     def init_fn(params):
-        return MuonState(new_count(0), zeros_like_tree(params), resolve_ns_coeffs(ns_coeffs, ns_steps), (),
-                         fresh_key(key))
+        # muon.py:207-223: momentum in mu_dtype (float32 by default).
+        return MuonState(new_count(0), zeros_like_tree(params, state_dtype(mu_dtype)),
+                         resolve_ns_coeffs(ns_coeffs, ns_steps), (), fresh_key(key))
 
     def update_fn(updates, state, params=None):
         dim_nums = _resolve_update_dimension_numbers(weight_dimension_numbers, params=params, updates=updates,
@@ -322,6 +337,7 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
         mus = tree_flatten(state.mu, is_leaf=is_aux_leaf)[0]
         count = host_count(state.count)
         ml = _gather_muon_leaves(leaves, mus, None, specs, "scale_by_muon")
+        ml, key_next = _seed_leaves(ml, state.key)
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=count, nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=state.ns_coeffs, ns_steps=ns_steps,
                                  lr=0.0, fuse_tail=0, preconditioning=preconditioning, adaptive=adaptive)
@@ -341,7 +357,7 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
         full = list(leaves)
         for L, o in zip(ml, outs):
             full[L.pos] = o
-        new_state = MuonState(safe_increment(state.count), state.mu, state.ns_coeffs, state.magma_s, state.key)
+        new_state = MuonState(safe_increment(state.count), state.mu, state.ns_coeffs, state.magma_s, key_next)
         return tree_unflatten(treedef, full), new_state
 
     return GradientTransformation(init_fn, update_fn)
@@ -437,6 +453,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             if g is not None:
                 _validate_matrix_operand(g, s, "scale_by_muon")
         ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon")
+        ml, muon_key_next = _seed_leaves(ml, muon_st.key)
         scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
         decays = []
         for L in ml:
@@ -473,6 +490,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             else:
                 a_items.append((g.contiguous(), amus[i], anus[i], None, out, 0.0, _lib.RF_F32))
             a_pos.append(i)
+        a_seeds, adam_key_next = adam_seeds(a_items, adam_st.key)
         if a_items:
             # The fallback leaves are independent of the Muon branch: with
             # pipelining they run on the aux stream, beside the last GEMMs.
@@ -484,7 +502,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             with torch.cuda.stream(side):
                 run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
                          count=host_count(adam_st.count), nesterov=nesterov, lr=alr,
-                         max_ctas_per_sm=SIDE_CTAS_PER_SM if side is not main else 0)
+                         max_ctas_per_sm=SIDE_CTAS_PER_SM if side is not main else 0, seeds=a_seeds)
             if side is not main:
                 main.wait_stream(side)
                 for it in a_items:
@@ -499,10 +517,10 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             full[i] = it[4]
 
         new_muon = MuonState(safe_increment(muon_st.count), muon_st.mu, muon_st.ns_coeffs, muon_st.magma_s,
-                             muon_st.key)
+                             muon_key_next)
         new_mlr = ScaleByScheduleState(safe_increment(mlr_state.count)) if callable(learning_rate) else mlr_state
         new_adam = ScaleByAdamState(safe_increment(adam_st.count), adam_st.mu, adam_st.nu, adam_st.magma_s,
-                                    adam_st.key)
+                                    adam_key_next)
         new_alr = ScaleByScheduleState(safe_increment(alr_state.count)) if callable(
             adam_learning_rate) else alr_state
         new_state = PartitionState({

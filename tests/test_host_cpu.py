@@ -156,8 +156,8 @@ def test_unsupported_options_fail_loudly():
         rf.scale_by_muon(preconditioning="nuclear")
     with pytest.raises(NotImplementedError, match="adaptive"):
         rf.scale_by_muon(adaptive=True, orthogonalize_fn=lambda x, *a: x)
-    with pytest.raises(NotImplementedError):
-        rf.muon(learning_rate=0.1, mu_dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError, match="mu_dtype"):
+        rf.muon(learning_rate=0.1, mu_dtype=torch.float16)  # float32 / bfloat16 state only
 
 
 def test_scale_by_muon_rejects_fallback_leaves():

@@ -359,3 +359,15 @@ def test_apply_updates_deterministic_and_unbiased():
     x = rng.standard_normal(1000).astype(np.float32)
     assert np.array_equal(O.apply_updates(x, x, "float32"), x + x)
     assert np.array_equal(O.apply_updates(x, x, "float16"), O.f16_round(x + x))
+
+
+def test_store_state_bf16_is_stochastic_rounding_of_the_float32_state():
+    # utils.py:412-425: bfloat16 state is the stochastic cast of the float32
+    # moment; float32 state is unchanged.
+    x = np.array([1.0 + 2.0 ** -8, -3.0, 2.0 ** -130, np.inf], np.float32)
+    assert np.array_equal(O.store_state(x, "float32"), x)
+    got = O.store_state(x, "bfloat16", seed=5)
+    n = O.noise16(5, 4)
+    assert np.array_equal(got, O.stochastic_round_bf16(x, n))
+    assert got[1] == -3.0 and got[3] == np.inf
+    assert got[0] in (1.0, 1.0078125)
