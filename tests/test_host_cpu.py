@@ -294,3 +294,31 @@ def test_key_seed_layouts():
     assert key_seed(7) == 7
     with pytest.raises(ValueError):
         key_seed([1, 2, 3])
+
+
+def test_state_dtype_and_init_trees():
+    from rollfast_b200.base import state_dtype
+
+    assert state_dtype(None) == torch.float32 and state_dtype("bf16") == torch.bfloat16
+    params = {"w": torch.zeros(8, 16), "b": torch.zeros(16)}
+    st = rf.muon(learning_rate=0.1, mu_dtype=torch.bfloat16).init(params)
+    muon_state = st.inner_states["muon"].inner_state[0][0]
+    adam_state = st.inner_states["adam"].inner_state[0]
+    assert muon_state.mu["w"].dtype == torch.bfloat16          # muon.py:207-223
+    assert adam_state.mu["b"].dtype == torch.bfloat16           # adam.py:98-112: both moments
+    assert adam_state.nu["b"].dtype == torch.bfloat16
+    st32 = rf.muon(learning_rate=0.1).init(params)
+    assert st32.inner_states["muon"].inner_state[0][0].mu["w"].dtype == torch.float32
+
+
+def test_sr_step_seeds_are_deterministic_and_advance_the_key():
+    from rollfast_b200.base import sr_step_seeds
+
+    k0 = torch.tensor([0, 42])
+    s1, k1 = sr_step_seeds(k0, 5)
+    s1b, k1b = sr_step_seeds(k0, 5)
+    assert s1 == s1b and torch.equal(k1, k1b)          # same key -> same streams
+    assert len(set(s1)) == 5                           # one stream per leaf
+    s2, k2 = sr_step_seeds(k1, 5)
+    assert not torch.equal(k1, k0) and set(s1).isdisjoint(s2)   # the next step draws new streams
+    assert k1.dtype == torch.int64 and k1.shape == (2,) and int(k1.max()) < 2 ** 32
