@@ -47,6 +47,7 @@ class ShardContext:
     plans: dict = field(default_factory=dict)
     comm_stream: object = None
     transport: str = "nccl"           # "ce" | "nccl" | "auto" (ce, else nccl)
+    owned_state: list = field(default_factory=list)  # [(momentum tensor, owner rank)] of the last update
 
     def close(self) -> None:
         """Releases the plans' peer mappings (collective when any exist)."""
@@ -282,6 +283,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         entry = (plan, buffers, gather)
         ctx.plans[key] = entry
     plan, buffers, gather = entry
+    ctx.owned_state = [(L.mu_state, plan.owner[i]) for i, L in enumerate(ml)]
     compute = torch.cuda.current_stream(dev)
     # Streams per rank: compute, tail, and either one copy stream (peer.py)
     # or the NCCL side stream, well inside the device's hardware queues.
@@ -385,6 +387,26 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     if trace is not None:
         trace.report(ctx.rank, [sum(sizes[i] for i in b.leaves) for b in plan.buckets])
     return _finish_leaves(ml)
+
+
+def consolidate_momentum(ctx: ShardContext | None = None) -> int:
+    """Make the Muon momentum current on every rank (collective over the
+    group), e.g. before saving a checkpoint from one rank.
+
+    A sharded update advances a leaf's momentum only on the rank that owns it;
+    everything else in the optimizer state (counts, keys, AdamW moments) is
+    replicated.  This broadcasts each leaf's momentum from its owner, as
+    recorded by the last sharded update, so afterwards every rank holds the
+    same full state.  Returns the number of leaves broadcast."""
+    import torch.distributed as dist
+
+    ctx = ctx or _ctx
+    if ctx is None or ctx.world_size == 1:
+        return 0
+    for t, owner in ctx.owned_state:
+        src = dist.get_global_rank(ctx.group, owner) if ctx.group is not None else owner
+        dist.broadcast(t, src=src, group=ctx.group)
+    return len(ctx.owned_state)
 
 
 def active_transport(ctx: ShardContext | None = None) -> str:

@@ -169,3 +169,42 @@ def test_gloo_world2_configure_transport_selection():
         assert res["ctx"] == (r, 2, "nccl", 3, "nccl")
         assert res["use"] == (True, True, "none")
         assert res["env"] == "ce" and res["cleared"]
+
+
+def _consolidate_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    import rollfast_b200.distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ctx = D.configure(transport="nccl")
+        owners = [0, 1, 1, 0, 1]
+        mus = [torch.full((3, 4), -1.0) for _ in owners]
+        for i, (t, o) in enumerate(zip(mus, owners)):
+            if o == rank:
+                t.fill_(10.0 * i + o)   # only the owner's copy is current
+        ctx.owned_state = list(zip(mus, owners))
+        n = D.consolidate_momentum()
+        ok = n == len(owners) and all(bool((t == 10.0 * i + o).all()) for i, (t, o) in enumerate(zip(mus, owners)))
+        D.clear()
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_world2_consolidate_momentum_from_owners():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_consolidate_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results == {0: True, 1: True}

@@ -66,6 +66,14 @@ def _worker(rank, world, port, transport, q):
             for k in params:
                 e = float(torch.linalg.vector_norm(u_sh[k] - u_ref[k]) / torch.linalg.vector_norm(u_ref[k]))
                 ok &= e <= 2e-3  # 16-bit gathered O vs fused fp32 O
+        # Momentum is current only on each leaf's owner until consolidated;
+        # then it equals the unsharded run's, bit for bit.
+        rf.distributed.consolidate_momentum(ctx)
+        mu_sh = sh_st.inner_states["muon"].inner_state[0][0].mu
+        mu_ref = ref_st.inner_states["muon"].inner_state[0][0].mu
+        for k, v in params.items():
+            if v.ndim >= 2:
+                ok &= bool(torch.equal(mu_sh[k], mu_ref[k]))
         rf.distributed.clear()
         q.put((rank, ok))
     except Exception as exc:  # report instead of hanging the other rank
