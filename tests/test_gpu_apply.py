@@ -73,3 +73,16 @@ def test_apply_stochastic_is_unbiased_and_keeps_specials():
     z = torch.zeros(8, dtype=torch.float32, device="cuda")
     out = rf.apply_updates({"w": sp}, {"w": z}, key=torch.tensor([1, 2]))["w"].float().cpu()
     assert out[0] == float("inf") and out[1] == -float("inf") and torch.isnan(out[2]) and out[3] == 0.0
+
+
+def test_reference_pure_bf16_apply_case():
+    # test_stochastic_rounding.py:81-99 (adamw entry): bf16 params and grads,
+    # stochastic apply keeps bf16.
+    import rollfast_b200 as rf
+
+    params = {"w": torch.ones((4, 4), dtype=torch.bfloat16, device="cuda")}
+    grads = {"w": torch.ones((4, 4), dtype=torch.bfloat16, device="cuda") * 0.1}
+    tx = rf.adamw(learning_rate=1e-3)
+    updates, _ = tx.update(grads, tx.init(params), params)
+    new = rf.apply_updates(params, updates, torch.tensor([0, 0]), stochastic=True)
+    assert new["w"].dtype == torch.bfloat16 and bool(torch.isfinite(new["w"].float()).all())

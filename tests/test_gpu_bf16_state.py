@@ -115,3 +115,15 @@ def test_hook_path_bf16_momentum():
     np.testing.assert_allclose(seen["d"], d, rtol=1e-6, atol=0)
     assert np.array_equal(st2.mu["w"].float().cpu().numpy(), O.store_state(mu_new, "bfloat16", seed))
     assert not torch.equal(st2.key, st.key)  # bf16 state consumes randomness: the key advances
+
+
+def test_reference_bf16_momentum_storage_case():
+    # test_muon.py:138-148: bf16 momentum state, finite updates.
+    import rollfast_b200 as rf
+
+    params = {"w": torch.ones((4, 4), device="cuda")}
+    grads = {"w": torch.ones((4, 4), device="cuda") * 0.1}
+    tx = rf.scale_by_muon(mu_dtype=torch.bfloat16, ns_steps=2)
+    updates, state = tx.update(grads, tx.init(params), params)
+    assert state.mu["w"].dtype == torch.bfloat16
+    assert bool(torch.isfinite(updates["w"]).all())
