@@ -14,8 +14,14 @@ Printed JSON (rank 0): ``value`` = ms per step (max over ranks, CUDA events),
 ``e2e`` = the same through host buffers (pinned gradients H2D + updates D2H
 inside the timed region), ``roofline`` = the Newton-Schulz tcgen05 GEMM
 kernel's algorithmic TFLOP/s (live per-launch CUDA events) against the
-measured bf16 peak, ``cpu_baseline`` = the NumPy restatement in ``oracle/``
-timed on this host's cores on one 4096x4096 leaf and extrapolated by FLOPs.
+measured bf16 peak, ``parity`` = one fresh step of the four Llama-3-8B matrix
+shapes checked against the NumPy oracle after the timed region (and, on more
+than one GPU, the sharded update against an unsharded recompute),
+``cpu_baseline`` = the NumPy restatement in ``oracle/`` timed on this host's
+cores on one layer (7 Muon leaves + 1/32 of the AdamW leaves) x 32.
+
+``--preconditioning``, ``--adaptive`` and ``--mu-dtype`` time the path's
+options on the same tree (the headline is the default, Frobenius / float32).
 """
 
 from __future__ import annotations
@@ -30,15 +36,34 @@ import sys
 import threading
 import time
 
-import numpy as np
-import torch
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# BLAS thread pools are sized when numpy is first imported, so rank 0 -- the
+# only rank that runs CPU work (the reference arm, the cpu_baseline leg and
+# the oracle side of the parity check) -- gets every host core here, before
+# that import.  torchrun exports OMP_NUM_THREADS=1 to every rank.
+if os.environ.get("RANK", "0") == "0":
+    for _var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_var] = str(host_threads())
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "Llama-3-8B Muon step ms at 1/2/4/8 B200; NS bf16 TFLOP/s vs peak"
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
-# ncu: 2-matrix capture, 15 stage launches of a 5-iteration NS = 6738 MB -> 449 MB per launch; x 48/2.
+# DRAM bytes per NS GEMM launch: one ncu capture of a 2-matrix 4096x14336
+# sub-batch read+wrote 6738 MB over the 15 stage launches of a 5-iteration NS
+# (449 MB per launch); the bench's launches hold 48 such matrices, whose
+# per-matrix working set exceeds L2, so the bytes scale by 48/2.
 TRAFFIC_PER_LAUNCH = round(6738e6 / 15 * 24)
 
 
@@ -172,29 +197,67 @@ class ClockSampler:
 # CPU baseline: the oracle (NumPy float32 restatement) on this host's cores.
 # ---------------------------------------------------------------------------
 
-def cpu_sample_ms(reps: int = 1):
-    """Time one full Muon step of a single 4096x4096 leaf on the oracle."""
-    import oracle as O
+LAYERS = 32
+LAYER_MATRICES = [("q", (4096, 4096)), ("k", (4096, 1024)), ("v", (4096, 1024)), ("o", (4096, 4096)),
+                  ("gate", (4096, 14336)), ("up", (4096, 14336)), ("down", (14336, 4096))]
+# One layer's share of the AdamW leaves: 1/32 of the embed and unembed rows,
+# its two RMSNorm vectors (the final norm, 1/8 of a layer's, is left out).
+ADAM_SLICE = {"embed": (128256 // LAYERS, 4096), "unembed": (128256 // LAYERS, 4096),
+              "attn_norm": (4096,), "mlp_norm": (4096,)}
+SAMPLE_KINDS = [k for k, _ in LAYER_MATRICES] + ["adamw"]
+CPU_SAMPLE_TEXT = ("oracle NumPy fp32 update of one Llama-3-8B layer (its 7 Muon leaves + 1/32 of the AdamW "
+                   "leaves, each a one-leaf oracle step with bf16 params), x 32")
 
-    rng = np.random.default_rng(0)
-    p = {"q": (rng.standard_normal((4096, 4096)) * 0.02).astype(np.float32)}
-    g = {"q": rng.standard_normal((4096, 4096)).astype(np.float32)}
-    ora = O.OracleMuon(learning_rate=0.02, weight_decay=0.01)
-    st = ora.init(p)
-    times = []
-    for _ in range(reps):
+
+class OracleLayerSample:
+    """The reference path restated in NumPy (``oracle/``, the checker) timed
+    on one Llama-3-8B layer: each of the layer's 7 Muon leaves, and its share
+    of the AdamW leaves, as one oracle step (fresh state, lr 0.02, wd 0.01,
+    beta 0.95, 5 standard NS iterations, bf16 parameter rounding)."""
+
+    def __init__(self, seed: int = 0):
+        import oracle as O
+
+        self.O = O
+        self.seed = seed
+
+    def _case(self, kind: str):
+        O = self.O
+        rng = np.random.default_rng(self.seed + SAMPLE_KINDS.index(kind))
+        shapes = dict(LAYER_MATRICES)
+        tree = {kind: shapes[kind]} if kind != "adamw" else ADAM_SLICE
+        specs = {k: None for k in tree} if kind == "adamw" else None
+        p = {k: O.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32)) for k, s in tree.items()}
+        g = {k: O.bf16_round(rng.standard_normal(s).astype(np.float32)) for k, s in tree.items()}
+        ora = O.OracleMuon(learning_rate=0.02, weight_decay=0.01, beta=0.95, muon_weight_dimension_numbers=specs)
+        return ora, ora.init(p), g, p, {k: "bfloat16" for k in tree}
+
+    def time_kind(self, kind: str) -> float:
+        ora, st, g, p, dts = self._case(kind)
         t0 = time.perf_counter()
-        _, st = ora.update(g, st, p, param_dtypes={"q": "bfloat16"})
-        times.append((time.perf_counter() - t0) * 1e3)
-    sample_flops = (4 * 4096 ** 3 + 2 * 4096 ** 3) * 5
-    return statistics.median(times), sample_flops
+        ora.update(g, st, p, param_dtypes=dts)
+        return (time.perf_counter() - t0) * 1e3
 
 
-def cores():
+def blas_threads() -> int | None:
+    """Threads of the BLAS pool numpy uses, as it reports them."""
     try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+        from threadpoolctl import threadpool_info
+
+        counts = [d.get("num_threads") for d in threadpool_info() if d.get("user_api") == "blas"]
+        return max(c for c in counts if c) if counts else None
+    except Exception:  # noqa: BLE001 - diagnostics only
+        return None
+
+
+def cpu_layer_baseline() -> dict:
+    """``cpu_baseline`` of our own line: every sample kind once."""
+    s = OracleLayerSample()
+    per = {k: s.time_kind(k) for k in SAMPLE_KINDS}
+    layer_ms = sum(per.values())
+    return {"value": round(LAYERS * layer_ms, 1), "unit": "ms", "cores": blas_threads() or host_threads(),
+            "kind": "port", "sample": f"{CPU_SAMPLE_TEXT} (one layer {layer_ms:.0f} ms)",
+            "per_leaf_ms": {k: round(v, 1) for k, v in per.items()}}
 
 
 # ---------------------------------------------------------------------------
@@ -209,32 +272,100 @@ def load_peaks():
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the oracle port on host cores (rank 0 only)."""
+    """--impl reference: the reference path's CPU restatement (the oracle
+    port; the reference itself needs JAX, which this image lacks) on every
+    host core, rank 0 only.  Each step times one leaf kind of one Llama-3-8B
+    layer (the 7 Muon matrices and the layer's AdamW share, in turn); the
+    reported step is 32 x the sum over kinds of each kind's median."""
     if rank != 0:
         return
-    n = cores()
-    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
-        os.environ.setdefault(var, str(n))
-    shapes = llama3_8b_shapes()
-    step_flops = ns_alg_flops(shapes)
-    samples = []
-    for i in range(args.warmup + args.steps):
-        ms, sflops = cpu_sample_ms(1)
+    s = OracleLayerSample()
+    n_timed = max(args.steps, len(SAMPLE_KINDS))
+    times = {k: [] for k in SAMPLE_KINDS}
+    for i in range(args.warmup + n_timed):
+        kind = SAMPLE_KINDS[i % len(SAMPLE_KINDS)]
+        ms = s.time_kind(kind)
         if i >= args.warmup:
-            samples.append(ms * step_flops / sflops)
-    val = statistics.median(samples)
+            times[kind].append(ms)
+    layer_ms = sum(statistics.median(v) for v in times.values())
+    val = LAYERS * layer_ms
+    threads = blas_threads() or host_threads()
     out = {
         "impl": "reference", "metric": METRIC, "value": round(val, 1), "unit": "ms",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(val, 1),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
-        "config": {"workload": "llama3_8b_muon_step", "sample": "one 4096x4096 leaf, extrapolated by NS FLOPs"},
-        "cpu_baseline": {"value": round(val, 1), "unit": "ms", "cores": n, "kind": "port",
-                         "sample": "oracle NumPy fp32 Muon step of one 4096x4096 leaf per step, x NS-FLOP ratio "
-                                   f"{step_flops / sflops:.1f}"},
+        "data": "synthetic: N(0,1) grads, N(0,0.02) params, bf16-rounded",
+        "config": {"workload": "llama3_8b_muon_step", "sample": "one layer x 32",
+                   "timed_samples": n_timed, "blas_threads": threads},
+        "cpu_baseline": {"value": round(val, 1), "unit": "ms", "cores": threads, "kind": "port",
+                         "sample": f"{CPU_SAMPLE_TEXT}; one leaf kind per step, median per kind "
+                                   f"(one layer {layer_ms:.0f} ms)",
+                         "per_leaf_ms": {k: round(statistics.median(v), 1) for k, v in times.items()}},
         "e2e": {"value": round(val, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
+
+
+PARITY_SHAPES = {"q": (4096, 4096), "k": (4096, 1024), "gate": (4096, 14336), "down": (14336, 4096),
+                 "norm": (4096,)}
+PARITY_TOL = {"muon": 1e-2, "adamw": 1e-6, "sharded": 1e-2}
+
+
+def parity_check(rf, dev, dist, rank: int, world: int) -> dict:
+    """One fresh step (lr 0.02, wd 0.01, beta 0.95, 5 standard iterations) of
+    a tree with the four Llama-3-8B matrix shapes and one AdamW vector, run
+    after the timed region.  Rank 0 compares the updates with the oracle
+    (NumPy float32) on the same inputs; on more than one GPU every rank runs
+    the sharded update and rank 0 also recomputes it unsharded."""
+    rng = np.random.default_rng(4321)
+    import oracle as O
+
+    p_np = {k: O.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32)) for k, s in PARITY_SHAPES.items()}
+    g_np = {k: O.bf16_round(rng.standard_normal(s).astype(np.float32)) for k, s in PARITY_SHAPES.items()}
+    to = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
+    params = {k: to(v) for k, v in p_np.items()}
+    grads = {k: to(v) for k, v in g_np.items()}
+
+    def step():
+        tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95)
+        u, _ = tx.update(grads, tx.init(params), params)
+        torch.cuda.synchronize()
+        return {k: v.float().cpu().numpy() for k, v in u.items()}
+
+    got = step()
+    out = {"leaves": {k: list(s) for k, s in PARITY_SHAPES.items()}, "tol": dict(PARITY_TOL),
+           "reference": "oracle NumPy fp32, one fresh step on the same bf16 inputs"}
+    if world > 1:
+        unsharded = None
+        if rank == 0:
+            prev = rf.distributed.use(None)
+            try:
+                unsharded = step()
+            finally:
+                rf.distributed.use(prev)
+        dist.barrier()
+        if rank == 0:
+            out["sharded_vs_unsharded"] = max(rel_err(got[k], unsharded[k]) for k in PARITY_SHAPES)
+    if rank == 0:
+        tx_o = O.OracleMuon(learning_rate=0.02, weight_decay=0.01, beta=0.95)
+        ref, _ = tx_o.update(g_np, tx_o.init(p_np), p_np, param_dtypes={k: "bfloat16" for k in PARITY_SHAPES})
+        errs = {k: rel_err(got[k], ref[k]) for k in PARITY_SHAPES}
+        out["rel_err"] = {k: float(f"{v:.3e}") for k, v in errs.items()}
+        out["max_rel_err_muon"] = max(v for k, v in errs.items() if k != "norm")
+        out["max_rel_err_adamw"] = errs["norm"]
+        ok = out["max_rel_err_muon"] <= PARITY_TOL["muon"] and out["max_rel_err_adamw"] <= PARITY_TOL["adamw"]
+        if world > 1:
+            ok = ok and out["sharded_vs_unsharded"] <= PARITY_TOL["sharded"]
+        out["pass"] = bool(ok)
+    if dist is not None:
+        dist.barrier()
+    return out
+
+
+def rel_err(a, b) -> float:
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
 def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
@@ -285,6 +416,10 @@ def main():
     ap.add_argument("--layers", type=int, default=32,
                     help="reduced-size case for kernel profiles only (the headline is 32 layers)")
     ap.add_argument("--vocab", type=int, default=128256)
+    ap.add_argument("--preconditioning", default="frobenius", choices=["frobenius", "aol", "schatten", "spectral"])
+    ap.add_argument("--adaptive", action="store_true")
+    ap.add_argument("--mu-dtype", default="float32", choices=["float32", "bfloat16"])
+    ap.add_argument("--no-parity", action="store_true")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -322,7 +457,14 @@ def main():
     params = map_shapes(shapes, lambda s: randn(s, 0.02))
     grad_sets = [map_shapes(shapes, lambda s: randn(s)) for _ in range(2)]
     specs = muon_specs(shapes, rf)
-    tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95, muon_weight_dimension_numbers=specs)
+    variant = {}
+    if args.preconditioning != "frobenius":
+        variant["preconditioning"] = args.preconditioning
+    if args.adaptive:
+        variant["adaptive"] = True
+    if args.mu_dtype != "float32":
+        variant["mu_dtype"] = torch.bfloat16
+    tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95, muon_weight_dimension_numbers=specs, **variant)
     state = tx.init(params)
     torch.cuda.synchronize()
 
@@ -376,13 +518,14 @@ def main():
             e2e = {"value": None, "unit": "ms", "unavailable": f"{type(exc).__name__}: {exc}"[:200]}
         grad_sets = None
 
+    # ---- parity of the same code path, after (outside) the timed region ---
+    del tx, state, params
+    torch.cuda.empty_cache()
+    parity = None if args.no_parity else parity_check(rf, dev, dist, rank, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n = cores()
-        s_ms, s_flops = cpu_sample_ms(1)
-        cpu = {"value": round(s_ms * ns_alg_flops(shapes) / s_flops, 1), "unit": "ms", "cores": n, "kind": "port",
-               "sample": f"oracle NumPy fp32 Muon step of one 4096x4096 leaf ({s_ms:.0f} ms), extrapolated by "
-                         "NS FLOPs to the full step"}
+        cpu = cpu_layer_baseline()
 
     if rank == 0:
         out = {
@@ -398,8 +541,9 @@ def main():
             "vs_baseline": None,
             "dtype": f"{args.precision} NS operands, fp32 accumulate/state, bf16 params+grads",
             "data": "synthetic: N(0,1) bf16 grads (2 seeded sets), N(0,0.02) bf16 params",
-            "config": {"workload": "llama3_8b_muon_step" if (args.layers, args.vocab) == (32, 128256)
-                       else f"reduced_{args.layers}_layers_vocab_{args.vocab}",
+            "config": {"workload": ("llama3_8b_muon_step" if (args.layers, args.vocab) == (32, 128256)
+                                    else f"reduced_{args.layers}_layers_vocab_{args.vocab}")
+                       + "".join(f"+{k}={v if k != 'mu_dtype' else args.mu_dtype}" for k, v in variant.items()),
                        "model": f"Llama-3-8B ({args.layers} layers) parameter set",
                        "muon_leaves": 7 * args.layers, "adam_leaves": 2 * args.layers + 3, "ns_steps": 5,
                        "ns_coeffs": "standard",
@@ -421,16 +565,14 @@ def main():
                 "launches": prof["launches"],
                 "gemm_ms_per_step": round(prof["gemm_ms"] / args.steps, 2),
                 # DRAM read+write bytes per launch of the 4096x14336 sub-batch
-                # stages (80% of the step's FLOPs), from the ncu capture in
-                # profiles/k_ns_tc2_4096x14336_b2.md: 449 MB per launch at 2
-                # matrices, scaled to the bench's 48-matrix launches (the
-                # per-matrix working set exceeds L2, so bytes grow with it).
+                # stages (80% of the step's FLOPs): see TRAFFIC_PER_LAUNCH.
                 "traffic": TRAFFIC_PER_LAUNCH if (args.layers, args.vocab) == (32, 128256) else None,
                 "traffic_unit": "bytes per launch",
             },
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "e2e": e2e,
+            "parity": parity,
             "cpu_baseline": cpu,
         }
         print(json.dumps(out), flush=True)

@@ -76,6 +76,10 @@ typedef struct rf_muon_leaf {
    * distribution, not bit for bit. */
   int32_t mu_dtype;
   uint64_t sr_seed;
+  /* 0: decay * p is rounded to the parameter dtype (optax add_decayed_weights
+   * with a Python-float weight decay, weakly typed); 1: formed in float32 (a
+   * schedule whose value is a float32 array, strongly typed). */
+  int32_t decay_in_f32;
 } rf_muon_leaf;
 
 /* Newton-Schulz preconditioning (orthogonalization.py:24, 153-176, 233-250). */
@@ -172,6 +176,7 @@ typedef struct rf_tail_leaf {
   int64_t n;
   int32_t o_dtype, param_dtype, out_dtype;
   float shape_scale, decay;
+  int32_t decay_in_f32;  /* as in rf_muon_leaf */
 } rf_tail_leaf;
 /* max_ctas_per_sm: 0 = default occupancy; 1-2 leaves room for a persistent
  * Newton-Schulz GEMM CTA on the same SM when this runs beside it. */
@@ -196,6 +201,10 @@ typedef struct rf_adam_leaf {
    * rounding (adam.py:219-222), noise streams from the two seeds. */
   int32_t state_dtype;
   uint64_t sr_seed_mu, sr_seed_nu;
+  /* Optional [n] element-wise decay mask (nonzero byte: decay this element),
+   * the array masks of the in-transform decay (utils.py:79-90, 173-197:
+   * where(mask, u + wd * p, u)); NULL: every element. */
+  const uint8_t* decay_mask;
 } rf_adam_leaf;
 typedef struct rf_adam_params {
   /* b1, b2 as the caller's double-precision scalars: the reference forms
@@ -282,6 +291,13 @@ rf_status rf_profile_end(double* gemm_ms, int64_t* launches, double* algorithmic
 /* Synchronises `stream`, then reports any sticky CUDA error or a bounded
  * device-side wait that gave up (RF_ETIMEOUT) since the last check. */
 rf_status rf_sync_check(void* stream);
+/* Non-blocking form of rf_sync_check's wait test: after the stream's prior
+ * work, copies the two device error words to dst[0] (a bounded wait in the
+ * tensor-core kernels gave up) and dst[1] (a cross-rank flag wait gave up);
+ * dst is 2 int32 of pinned host or device memory.  A nonzero word means the
+ * results of work before it are invalid; rf_sync_check then reports
+ * RF_ETIMEOUT and clears the words.  Nothing is cleared here. */
+rf_status rf_error_snapshot(int32_t* dst, void* stream);
 
 #ifdef __cplusplus
 }

@@ -44,7 +44,9 @@ __all__ = [
     "momentum_runtime",
     "shape_scale_factor",
     "adam_leaf_update",
+    "decay_at",
     "decay_term",
+    "in_transform_decay",
     "OracleMuon",
     "bf16_round",
     "f16_round",
@@ -557,6 +559,24 @@ def decay_term(p: np.ndarray, wd: float, param_dtype: str) -> np.ndarray:
     return (np.float32(wd) * pf).astype(np.float32)
 
 
+def decay_at(weight_decay, count: int):
+    """(value, weak) of a scalar-or-schedule weight decay at ``count``
+    (utils.py:93-102).  Under JAX's promotion rules a Python scalar is weakly
+    typed (``weight_decay * p`` forms in the parameter dtype); a NumPy scalar
+    or array value is strongly typed float32 (the product forms in float32)."""
+    v = weight_decay(count) if callable(weight_decay) else weight_decay
+    return float(v), type(v) in (int, float)
+
+
+def in_transform_decay(u: np.ndarray, p: np.ndarray, wd_step: float, mask=True) -> np.ndarray:
+    """utils.py:79-90: ``where(mask, u + wd * p.astype(u.dtype), u)`` with the
+    float32 update (the product forms in float32); ``mask`` a boolean or an
+    array broadcast against the leaf."""
+    uf = np.asarray(u, np.float32)
+    dec = (uf + (np.float32(wd_step) * np.asarray(p, np.float32)).astype(np.float32)).astype(np.float32)
+    return np.where(np.asarray(mask, dtype=bool), dec, uf).astype(np.float32)
+
+
 def adam_leaf_update(g, mu, nu, count: int, *, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0,
                      nesterov=False, dtype=np.float32):
     """adam.py:123-177 (no Magma, in-transform decay 0): returns
@@ -641,6 +661,10 @@ class OracleMuon:
             wd_mask = tree_map(lambda p: True, params)
         count = state["count"]
         lr = self.lr(count) if callable(self.lr) else self.lr
+        # add_decayed_weights of each branch, a constant or a schedule at the
+        # branch's step count (every transform of a chain counts alike).
+        mwd, mweak = decay_at(self.wd, count)
+        awd, aweak = decay_at(self.adam_wd, state["adam_count"])
         adam_lr = self.adam_lr(state["adam_count"]) if callable(self.adam_lr) else self.adam_lr
         coeffs = state["ns_coeffs"]
         dt = self.dtype
@@ -660,16 +684,16 @@ class OracleMuon:
                 if self.adaptive:  # muon.py:272-282: <mu_hat, O> O over the whole leaf
                     o = (np.sum(d.astype(dt) * o, dtype=dt) * o).astype(dt)
                 u = (o * shape_scale_factor(np.shape(g), spec, self.consistent_rms)).astype(dt)
-                if self.wd != 0.0 and msk:
-                    u = (u + decay_term(p, self.wd, pdt)).astype(dt)
+                if mwd != 0.0 and msk:
+                    u = (u + decay_term(p, mwd, pdt if mweak else "float32")).astype(dt)
                 return (dt(-lr) * u).astype(dt)
             u, am_new, an_new = adam_leaf_update(g, am, an, state["adam_count"], b1=self.b1,
                                                  b2=self.b2, eps=self.adam_eps,
                                                  eps_root=self.adam_eps_root,
                                                  nesterov=self.nesterov, dtype=dt)
             new_am[key], new_an[key] = am_new, an_new
-            if self.adam_wd != 0.0 and msk:
-                u = (u + decay_term(p, self.adam_wd, pdt)).astype(dt)
+            if awd != 0.0 and msk:
+                u = (u + decay_term(p, awd, pdt if aweak else "float32")).astype(dt)
             return (dt(-adam_lr) * u).astype(dt)
 
         flat_g = tree_leaves_with_path(grads)

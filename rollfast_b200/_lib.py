@@ -41,6 +41,7 @@ EXPORTED = (
     "rf_version",
     "rf_kernel_launch_count",
     "rf_sync_check",
+    "rf_error_snapshot",
     "rf_profile_begin",
     "rf_profile_end",
     "rf_apply_updates",
@@ -86,6 +87,7 @@ class RfMuonLeaf(ctypes.Structure):
         ("skip_ns", ctypes.c_int32),
         ("mu_dtype", ctypes.c_int32),
         ("sr_seed", ctypes.c_uint64),
+        ("decay_in_f32", ctypes.c_int32),
     ]
 
 
@@ -120,6 +122,7 @@ class RfTailLeaf(ctypes.Structure):
         ("out_dtype", ctypes.c_int32),
         ("shape_scale", ctypes.c_float),
         ("decay", ctypes.c_float),
+        ("decay_in_f32", ctypes.c_int32),
     ]
 
 
@@ -139,6 +142,7 @@ class RfAdamLeaf(ctypes.Structure):
         ("state_dtype", ctypes.c_int32),
         ("sr_seed_mu", ctypes.c_uint64),
         ("sr_seed_nu", ctypes.c_uint64),
+        ("decay_mask", ctypes.c_void_p),
     ]
 
 
@@ -187,6 +191,7 @@ def load(path: str | None = None):
         lib.rf_kernel_launch_count.restype = i64
         lib.rf_kernel_launch_count.argtypes = []
         lib.rf_sync_check.argtypes = [vp]
+        lib.rf_error_snapshot.argtypes = [vp, vp]
         lib.rf_profile_begin.argtypes = []
         lib.rf_profile_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i64),
                                        ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
@@ -235,6 +240,11 @@ def kernel_launch_count() -> int:
 
 def sync_check(stream_handle: int) -> None:
     check(load().rf_sync_check(ctypes.c_void_p(stream_handle)))
+
+
+def error_snapshot(dst_ptr: int, stream_handle: int) -> None:
+    """Enqueue a copy of the two device error words to ``dst_ptr`` (2 int32)."""
+    check(load().rf_error_snapshot(ctypes.c_void_p(dst_ptr), ctypes.c_void_p(stream_handle)))
 
 
 def profile_begin() -> None:

@@ -11,6 +11,7 @@ from . import _lib
 from .base import (
     AddDecayedWeightsState,
     GradientTransformation,
+    decay_at,
     MaskedState,
     ScaleByScheduleState,
     ScaleState,
@@ -57,13 +58,17 @@ def zeros_like_tree(params, dtype=torch.float32):
 
 def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float,
              max_ctas_per_sm: int = 0, seeds=None) -> None:
-    """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype);
-    ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state."""
+    """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype[, mask]);
+    ``mask``: an optional uint8 tensor shaped like g (element-wise decay
+    mask); ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state."""
     if not items:
         return
     lib = _lib.load()
     arr = (_lib.RfAdamLeaf * len(items))()
-    for i, (g, mu, nu, p, out, decay, rdt) in enumerate(items):
+    for i, item in enumerate(items):
+        g, mu, nu, p, out, decay, rdt = item[:7]
+        mask = item[7] if len(item) > 7 else None
+        arr[i].decay_mask = mask.data_ptr() if mask is not None else None
         arr[i].grad = g.data_ptr()
         arr[i].mu = mu.data_ptr()
         arr[i].nu = nu.data_ptr()
@@ -84,8 +89,21 @@ def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: fl
                                    torch.cuda.current_stream(items[0][0].device).cuda_stream))
 
 
-def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_rounding_param: bool):
-    """Leaf list for run_adam plus the output tree skeleton."""
+def _elementwise_mask(m, g: torch.Tensor) -> torch.Tensor:
+    """An array mask broadcast to the leaf's shape, as one byte per element."""
+    t = torch.as_tensor(m, device=g.device)
+    return t.to(torch.bool).expand(g.shape).contiguous().to(torch.uint8)
+
+
+def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_rounding_param: bool,
+                decay_weak: bool = True):
+    """Leaf list for run_adam plus the output tree skeleton.
+
+    ``decay_rounding_param``: the decay of optax.add_decayed_weights (per-leaf
+    boolean masks; ``weight_decay * p`` in the parameter dtype when
+    ``decay_weak``, else float32); otherwise the in-transform decay of
+    scale_by_adam (utils.py:79-90: float32 product, array masks applied
+    element-wise)."""
     leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
     mus = tree_flatten(state.mu, is_leaf=is_aux_leaf)[0]
     nus = tree_flatten(state.nu, is_leaf=is_aux_leaf)[0]
@@ -99,18 +117,38 @@ def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_round
         require_cuda(g, "gradient")
         if g.dtype.is_complex:
             raise NotImplementedError("complex leaves are not on the B200 hot path")
-        if isinstance(m, torch.Tensor) and m.ndim > 0:
-            raise NotImplementedError("element-wise weight-decay masks are not supported; use per-leaf booleans")
-        use = decay != 0.0 and bool(m) and p is not None and not is_aux_leaf(p)
+        elementwise = not isinstance(m, bool) and getattr(m, "ndim", 0) > 0
+        if elementwise and decay_rounding_param:
+            raise ValueError("The truth value of an array with more than one element is ambiguous: "
+                             "add_decayed_weights masks take one boolean per leaf.")
+        use = decay != 0.0 and (elementwise or bool(m)) and p is not None and not is_aux_leaf(p)
         out = torch.empty(g.shape, dtype=torch.float32, device=g.device)
         if use:
-            rdt = rf_dtype(p) if decay_rounding_param else _lib.RF_F32
-            d = round_to_dtype(decay, p.dtype) if decay_rounding_param else decay
-            items.append((g.contiguous(), mu, nu, p.contiguous(), out, d, rdt))
+            weak = decay_rounding_param and decay_weak
+            rdt = rf_dtype(p) if weak else _lib.RF_F32
+            d = round_to_dtype(decay, p.dtype) if weak else decay
+            items.append((g.contiguous(), mu, nu, p.contiguous(), out, d, rdt,
+                          _elementwise_mask(m, g) if elementwise else None))
         else:
             items.append((g.contiguous(), mu, nu, None, out, 0.0, _lib.RF_F32))
         outs.append(out)
     return items, outs, treedef
+
+
+def wd_count(st) -> int:
+    """Step count of an add_decayed_weights state (0 for a constant decay)."""
+    inner = st.inner_state if isinstance(st, MaskedState) else st
+    return 0 if inner.count is None else host_count(inner.count)
+
+
+def bump_wd_state(st):
+    """The add_decayed_weights state after one update (a scheduled decay's
+    count advances; a constant decay's state is empty)."""
+    if isinstance(st, MaskedState):
+        return MaskedState(bump_wd_state(st.inner_state))
+    if isinstance(st, AddDecayedWeightsState) and st.count is not None:
+        return AddDecayedWeightsState(safe_increment(st.count))
+    return st
 
 
 def adam_seeds(items, key):
@@ -131,8 +169,6 @@ def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, we
     if use_magma:
         raise NotImplementedError("Magma masking is not on the B200 hot path")
     sdt = state_dtype(mu_dtype)
-    if callable(weight_decay):
-        raise NotImplementedError("scheduled weight_decay is not supported")
 
     def init_fn(params):
         # adam.py:98-112: both moments in mu_dtype (float32 by default).
@@ -147,7 +183,9 @@ def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, we
             )
         count = host_count(state.count)
         mask = resolve_mask(weight_decay_mask, params) if params is not None else None
-        items, outs, treedef = _adam_items(updates, state, params, decay=float(weight_decay), decay_mask=mask,
+        # adam.py:185-201: the decay at the transform's count (utils.py:93-102).
+        wd_step, _ = decay_at(weight_decay, count)
+        items, outs, treedef = _adam_items(updates, state, params, decay=wd_step, decay_mask=mask,
                                            decay_rounding_param=False)
         seeds, key_next = adam_seeds(items, state.key)
         run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=count, nesterov=nesterov, lr=-1.0,
@@ -168,14 +206,13 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
     if use_magma:
         raise NotImplementedError("Magma masking is not on the B200 hot path")
     state_dtype(mu_dtype)  # validates
-    if callable(weight_decay):
-        raise NotImplementedError("scheduled weight_decay is not supported")
+    scheduled = callable(weight_decay)
     inner = scale_by_adam(b1, b2, eps, eps_root, mu_dtype, nesterov=nesterov, key=key)
 
     def init_fn(params):
         states = [inner.init(params)]
         if decay_on:
-            wd_state = AddDecayedWeightsState()
+            wd_state = AddDecayedWeightsState(new_count(0)) if scheduled else AddDecayedWeightsState()
             states.append(MaskedState(wd_state) if weight_decay_mask is not None else wd_state)
         states.append(ScaleByScheduleState(new_count(0)) if callable(learning_rate) else ScaleState())
         return tuple(states)
@@ -191,16 +228,17 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
         lr = resolve_scalar(learning_rate, host_count(lr_state.count)) if callable(learning_rate) else float(
             learning_rate)
         mask = resolve_mask(weight_decay_mask, params) if (decay_on and params is not None) else None
-        items, outs, treedef = _adam_items(updates, adam_state, params,
-                                           decay=float(weight_decay) if decay_on else 0.0, decay_mask=mask,
-                                           decay_rounding_param=True)
+        wd, weak = decay_at(weight_decay, host_count(wd_count(state[1]))) if decay_on else (0.0, True)
+        items, outs, treedef = _adam_items(updates, adam_state, params, decay=wd, decay_mask=mask,
+                                           decay_rounding_param=True, decay_weak=weak)
         seeds, key_next = adam_seeds(items, adam_state.key)
         run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=host_count(adam_state.count),
                  nesterov=nesterov, lr=lr, seeds=seeds)
         new_adam = ScaleByAdamState(safe_increment(adam_state.count), adam_state.mu, adam_state.nu,
                                     adam_state.magma_s, key_next)
         new_lr = ScaleByScheduleState(safe_increment(lr_state.count)) if callable(learning_rate) else lr_state
-        return tree_unflatten(treedef, outs), (new_adam, *state[1:-1], new_lr)
+        rest = [bump_wd_state(s) for s in state[1:-1]]
+        return tree_unflatten(treedef, outs), (new_adam, *rest, new_lr)
 
     return GradientTransformation(init_fn, update_fn)
 

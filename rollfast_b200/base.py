@@ -48,7 +48,11 @@ class ScaleByScheduleState(NamedTuple):
 
 
 class AddDecayedWeightsState(NamedTuple):
-    """State of ``optax.add_decayed_weights``."""
+    """State of ``optax.add_decayed_weights``: empty (``count`` None) for a
+    constant weight decay; for a scheduled one, the step count the schedule
+    is evaluated at (0 on the first update)."""
+
+    count: Any = None
 
 
 class MaskedState(NamedTuple):
@@ -121,6 +125,20 @@ def require_cuda(t: torch.Tensor, what: str) -> None:
 def resolve_scalar(value: ScalarOrSchedule, count: int) -> float:
     """utils.py:93-102."""
     return float(value(count)) if callable(value) else float(value)
+
+
+def decay_at(weight_decay: ScalarOrSchedule, count: int) -> tuple[float, bool]:
+    """Weight decay at ``count`` and whether it is weakly typed.
+
+    A Python scalar (a constant, or a schedule that returns one) is weakly
+    typed under JAX's promotion rules, so ``weight_decay * p`` is formed in
+    the parameter dtype; a schedule that returns an array or a NumPy scalar
+    (a float32 value, as Optax schedules computed from the int32 step count
+    return) is strongly typed and the product is formed in float32."""
+    if not callable(weight_decay):
+        return float(weight_decay), True
+    v = weight_decay(count)
+    return float(v), type(v) in (int, float)
 
 
 def has_nonzero_or_scheduled(value: ScalarOrSchedule) -> bool:
@@ -237,12 +255,14 @@ SIDE_CTAS_PER_SM = 2  # occupancy of HBM-bound kernels run beside the persistent
 
 
 def run_tail(items, lr: float, max_ctas_per_sm: int = 0) -> None:
-    """items: list of (u, p_or_None, out, shape_scale, decay)."""
+    """items: list of (u, p_or_None, out, shape_scale, decay[, decay_in_f32])."""
     if not items:
         return
     lib = _lib.load()
     arr = (_lib.RfTailLeaf * len(items))()
-    for i, (u, p, out, scale, decay) in enumerate(items):
+    for i, item in enumerate(items):
+        u, p, out, scale, decay = item[:5]
+        arr[i].decay_in_f32 = int(bool(item[5])) if len(item) > 5 else 0
         arr[i].o = u.data_ptr()
         arr[i].param = p.data_ptr() if p is not None else None
         arr[i].out = out.data_ptr()
@@ -292,15 +312,20 @@ def scale_by_learning_rate(learning_rate: ScalarOrSchedule, *, flip_sign: bool =
     return GradientTransformation(init_fn, update_fn)
 
 
-def add_decayed_weights(weight_decay: float = 0.0, mask=None) -> GradientTransformation:
-    """optax.add_decayed_weights: ``u + weight_decay * p`` where the product is
-    formed in the parameter dtype (JAX weak typing of the Python float)."""
-    if callable(weight_decay):
-        raise NotImplementedError("scheduled weight_decay in add_decayed_weights is not supported")
+def add_decayed_weights(weight_decay: ScalarOrSchedule = 0.0, mask=None) -> GradientTransformation:
+    """optax.add_decayed_weights: ``u + weight_decay * p``.  A constant (Python
+    float) weight decay forms the product in the parameter dtype (JAX weak
+    typing); a schedule is evaluated at the transform's own step count, kept
+    in its state, and its product's dtype follows ``decay_at``."""
+    scheduled = callable(weight_decay)
+
+    def init_fn(params):
+        return AddDecayedWeightsState(new_count(0)) if scheduled else AddDecayedWeightsState()
 
     def update_fn(updates, state, params=None, **extra):
         if params is None:
             raise ValueError(NO_PARAMS_MSG)
+        wd, weak = decay_at(weight_decay, host_count(state.count) if scheduled else 0)
         leaves, treedef = _array_leaves(updates)
         pleaves = tree_flatten(params, is_leaf=is_aux_leaf)[0]
         items, outs = [], []
@@ -309,13 +334,16 @@ def add_decayed_weights(weight_decay: float = 0.0, mask=None) -> GradientTransfo
                 outs.append(u)
                 continue
             require_cuda(u, "update")
-            o = torch.empty(u.shape, dtype=torch.promote_types(u.dtype, p.dtype), device=u.device)
-            items.append((u.contiguous(), p.contiguous(), o, 1.0, round_to_dtype(weight_decay, p.dtype)))
+            o = torch.empty(u.shape, dtype=torch.promote_types(u.dtype, p.dtype if weak else torch.float32),
+                            device=u.device)
+            items.append((u.contiguous(), p.contiguous(), o, 1.0, round_to_dtype(wd, p.dtype) if weak else wd,
+                          not weak))
             outs.append(o)
         run_tail(items, -1.0)
-        return tree_unflatten(treedef, outs), state
+        new_state = AddDecayedWeightsState(safe_increment(state.count)) if scheduled else state
+        return tree_unflatten(treedef, outs), new_state
 
-    tx = GradientTransformation(lambda params: AddDecayedWeightsState(), update_fn)
+    tx = GradientTransformation(init_fn, update_fn)
     if mask is not None:
         return masked(tx, mask)
     return tx

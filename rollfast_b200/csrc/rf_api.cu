@@ -56,6 +56,8 @@ int num_sms() {
 
 rf_status take_device_error();  // rf_ns_tc.cu
 rf_status take_peer_error();    // rf_peer.cu
+rf_status snapshot_device_error(int32_t* dst, cudaStream_t st);  // rf_ns_tc.cu
+rf_status snapshot_peer_error(int32_t* dst, cudaStream_t st);    // rf_peer.cu
 
 // ---------------------------------------------------------------------------
 // Host-side scalar factors, formed in float32 like the reference.
@@ -96,6 +98,7 @@ struct LeafPlan {
   int transposed;
   int gdt, pdt, odt;
   float shape_scale, decay;
+  int decay_dt;         // dtype decay * p is rounded to
   int64_t scale_index;  // first matrix in the scale array
   int mu_bf16;          // momentum stored as bfloat16 (stochastic rounding)
   uint64_t sr_seed;
@@ -343,6 +346,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         f.p_dtype = lp.pdt;
         f.shape_scale = lp.shape_scale;
         f.decay = lp.decay;
+        f.decay_dt = lp.decay_dt;
         // Runs of 32 along the leaf's rows: length n (NS columns) for a
         // plain leaf, m (NS rows) for a transposed one.
         f.vec_ok = ((lp.transposed ? gp.m : gp.n) % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
@@ -458,6 +462,7 @@ static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vec
     p.odt = l.out_dtype;
     p.shape_scale = l.shape_scale;
     p.decay = l.decay;
+    p.decay_dt = l.decay_in_f32 ? RF_F32 : p.pdt;
     p.mu_bf16 = l.mu_dtype == RF_BF16;
     p.sr_seed = l.sr_seed;
     out.push_back(p);
@@ -498,6 +503,13 @@ rf_status rf_sync_check(void* stream) {
   if (e != cudaSuccess) return fail(RF_ECUDA, std::string("stream sync: ") + cudaGetErrorString(e));
   RF_TRY(take_peer_error());
   return take_device_error();
+}
+
+rf_status rf_error_snapshot(int32_t* dst, void* stream) {
+  if (!dst) return fail(RF_EINVAL, "null output pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  RF_TRY(snapshot_device_error(dst, st));
+  return snapshot_peer_error(dst + 1, st);
 }
 
 rf_status rf_muon_workspace_size(const rf_muon_leaf* leaves, int32_t n_leaves, int32_t precision, int32_t pipelined,
@@ -552,6 +564,7 @@ static rf_status adaptive_pass(const Plan& P, const MomentumCoeffs& mc, int fuse
       t.pdt = lp.p ? lp.pdt : RF_F32;
       t.shape_scale = fuse_tail ? lp.shape_scale : 1.f;
       t.decay = fuse_tail ? lp.decay : 0.f;
+      t.decay_dt = lp.decay_dt;
       t.dev_scale = ip + i;
       t.vec_ok = (n % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
                  (!t.p || reinterpret_cast<uintptr_t>(lp.p) % 16 == 0);
@@ -660,6 +673,7 @@ static rf_status ns_plan(int64_t batch, int64_t rows, int64_t cols, int32_t prec
   l.odt = out_dtype;
   l.shape_scale = 1.f;
   l.decay = 0.f;
+  l.decay_dt = RF_F32;
   return build_plan({l}, precision, P);
 }
 
@@ -749,6 +763,7 @@ rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, i
       d.outdt = l.out_dtype;
       d.shape_scale = l.shape_scale;
       d.decay = l.decay;
+      d.decay_dt = l.decay_in_f32 ? RF_F32 : d.pdt;
       d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.o) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&
                  (!l.param || reinterpret_cast<uintptr_t>(l.param) % 16 == 0);
@@ -813,10 +828,12 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
       d.sdt = l.state_dtype;
       d.seed_mu = l.sr_seed_mu;
       d.seed_nu = l.sr_seed_nu;
+      d.mask = l.decay != 0.f ? l.decay_mask : nullptr;
       d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.nu) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&
-                 (!l.param || reinterpret_cast<uintptr_t>(l.param) % 16 == 0);
+                 (!l.param || reinterpret_cast<uintptr_t>(l.param) % 16 == 0) &&
+                 (!d.mask || reinterpret_cast<uintptr_t>(d.mask) % 8 == 0);
       if (l.decay != 0.f && !valid_dtype(l.decay_rounding)) return fail(RF_EINVAL, "adam leaf: bad decay_rounding");
       chunks += ceil_div(l.n, kChunk);
     }

@@ -61,10 +61,12 @@ __device__ __forceinline__ float round_to(int dt, float v) {
 }
 
 // Optax add_decayed_weights forms `weight_decay * p` with a weakly typed
-// Python float, i.e. in the parameter dtype; `decay` arrives already rounded
-// to that dtype by the host.
-__device__ __forceinline__ float decay_term(int pdt, float decay, float p) {
-  return round_to(pdt, decay * p);
+// Python float, i.e. in the parameter dtype (`decay` arrives already rounded
+// to that dtype by the host); a strongly typed float32 weight decay (a
+// schedule's array value, or the in-transform decay of scale_by_adam) forms
+// it in float32 (rdt = RF_F32).
+__device__ __forceinline__ float decay_term(int rdt, float decay, float p) {
+  return round_to(rdt, decay * p);
 }
 
 inline size_t dtype_size(int dt) { return dt == RF_F32 ? 4 : 2; }

@@ -424,7 +424,7 @@ __device__ __forceinline__ void st8(void* p, int dt, int64_t i, const float* v) 
 }
 
 __device__ __forceinline__ float adam_one(const AdamCoeffs& c, const AdamLeafDev& L, float g, float& mu, float& nu,
-                                          float p) {
+                                          float p, bool decay_on) {
   mu = __fadd_rn(__fmul_rn(c.one_minus_b1, g), __fmul_rn(c.b1, mu));
   nu = __fadd_rn(__fmul_rn(c.one_minus_b2, __fmul_rn(g, g)), __fmul_rn(c.b2, nu));
   float mh;
@@ -435,7 +435,7 @@ __device__ __forceinline__ float adam_one(const AdamCoeffs& c, const AdamLeafDev
   }
   const float nh = __fdiv_rn(nu, c.bc2);
   float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(__fadd_rn(nh, c.eps_root)), c.eps));
-  if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, p));
+  if (decay_on) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, p));
   return __fmul_rn(c.neg_lr, u);
 }
 
@@ -459,8 +459,12 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
         ld8(L.mu, L.sdt, i, mu);
         ld8(L.nu, L.sdt, i, nu);
         if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
+        uint2 mk = make_uint2(0x01010101u, 0x01010101u);
+        if (L.mask) mk = *reinterpret_cast<const uint2*>(L.mask + i);
+        const uint8_t* mb = reinterpret_cast<const uint8_t*>(&mk);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) u[k] = adam_one(c, L, g[k], mu[k], nu[k], L.decay != 0.f ? p[k] : 0.f);
+        for (int k = 0; k < 8; ++k)
+          u[k] = adam_one(c, L, g[k], mu[k], nu[k], L.decay != 0.f ? p[k] : 0.f, L.decay != 0.f && mb[k] != 0);
         if (L.sdt == RF_BF16) {  // adam.py:219-222: both moments stochastically rounded
           sr_store8_bf16(L.mu, i, mu, L.seed_mu);
           sr_store8_bf16(L.nu, i, nu, L.seed_nu);
@@ -475,7 +479,7 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
         const float g = ld_as_float(L.g, L.gdt, i);
         float mu = ld_as_float(L.mu, L.sdt, i), nu = ld_as_float(L.nu, L.sdt, i);
         const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
-        const float u = adam_one(c, L, g, mu, nu, p);
+        const float u = adam_one(c, L, g, mu, nu, p, L.decay != 0.f && (!L.mask || L.mask[i] != 0));
         if (L.sdt == RF_BF16) {
           sr_store1_bf16(L.mu, i, mu, L.seed_mu);
           sr_store1_bf16(L.nu, i, nu, L.seed_nu);
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(kEwThreads) k_direction(const __grid_constant_
 // ds: the adaptive factor <d, O> (1 otherwise, which leaves o unchanged).
 __device__ __forceinline__ float tail_one(const TailLeafDev& L, float neg_lr, float o, float p, float ds) {
   float u = __fmul_rn(__fmul_rn(ds, o), L.shape_scale);
-  if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.pdt, L.decay, p));
+  if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, p));
   return __fmul_rn(neg_lr, u);
 }
 

@@ -92,10 +92,11 @@ struct AdamLeafDev {
   void* out;
   int64_t n, chunk_begin;
   int32_t gdt, pdt, odt, decay_dt;
-  int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
+  int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0 (and an 8-byte aligned mask)
   float decay;
   int32_t sdt;     // moment storage dtype: RF_F32, or RF_BF16 (stochastic rounding)
   uint64_t seed_mu, seed_nu;
+  const uint8_t* mask;  // optional element-wise decay mask
 };
 struct AdamLaunch {
   AdamLeafDev leaf[kMaxLeavesPerLaunch];
@@ -130,6 +131,7 @@ struct TailLeafDev {
   int32_t vec_ok;  // 16-byte aligned buffers, n % 8 == 0
   float shape_scale, decay;
   const float* dev_scale;  // optional device factor applied to O first (adaptive)
+  int32_t decay_dt;        // dtype decay * p is rounded to
 };
 struct TailLaunch {
   TailLeafDev leaf[kMaxLeavesPerLaunch];
@@ -158,6 +160,7 @@ struct FinalLeaf {
   int32_t out_dtype, p_dtype;
   int32_t vec_ok;  // out / p 16-byte aligned and the leaf's row length % 8 == 0: vector epilogue
   float shape_scale, decay;
+  int32_t decay_dt;  // dtype decay * p is rounded to (the parameter dtype, or RF_F32)
 };
 
 struct NsGemmArgs {
@@ -277,7 +280,7 @@ __device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf
   float v = o;
   if (a.fuse_tail) {
     v = __fmul_rn(o, L.shape_scale);
-    if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.p_dtype, L.decay, ld_as_float(L.p, L.p_dtype, idx)));
+    if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.decay_dt, L.decay, ld_as_float(L.p, L.p_dtype, idx)));
     v = __fmul_rn(a.neg_lr, v);
   }
   st_from_float(L.out, L.out_dtype, idx, v);
@@ -325,7 +328,7 @@ __device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const Fin
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       float u = __fmul_rn(v[k], L.shape_scale);
-      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.p_dtype, L.decay, pv[k]));
+      if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, pv[k]));
       v[k] = __fmul_rn(a.neg_lr, u);
     }
   }

@@ -1020,4 +1020,11 @@ rf_status take_device_error() {
   return RF_OK;
 }
 
+// Stream-ordered copy of the tensor-core kernels' error word to *dst.
+rf_status snapshot_device_error(int32_t* dst, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(dst, g_tc_error, sizeof(int), 0, cudaMemcpyDefault, st);
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string("copying device error word: ") + cudaGetErrorString(e));
+  return RF_OK;
+}
+
 }  // namespace rf

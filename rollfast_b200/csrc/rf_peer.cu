@@ -124,6 +124,13 @@ rf_status take_peer_error() {
   return RF_OK;
 }
 
+// Stream-ordered copy of the peer error word to *dst (host or device memory).
+rf_status snapshot_peer_error(int32_t* dst, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(dst, peer::g_peer_error, sizeof(int), 0, cudaMemcpyDefault, st);
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string("copying peer error word: ") + cudaGetErrorString(e));
+  return RF_OK;
+}
+
 }  // namespace rf
 
 using namespace rf;

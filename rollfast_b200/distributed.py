@@ -48,6 +48,8 @@ class ShardContext:
     comm_stream: object = None
     transport: str = "nccl"           # "ce" | "nccl" | "auto" (ce, else nccl)
     owned_state: list = field(default_factory=list)  # [(momentum tensor, owner rank)] of the last update
+    errors: "ErrorWatch" = None
+    steps: int = 0                    # sharded updates run with this context
 
     def close(self) -> None:
         """Releases the plans' peer mappings (collective when any exist)."""
@@ -56,6 +58,55 @@ class ShardContext:
             if gather is not None:
                 gather.close()
         self.plans.clear()
+
+
+class ErrorWatch:
+    """Bounded device-side waits of the sharded update (cross-rank flag waits,
+    the tensor-core kernels' pipeline waits) that give up set an error word
+    instead of hanging; the results of that step are then invalid.
+
+    After every sharded step the two words are copied, stream-ordered, into a
+    small pinned host buffer (``rf_error_snapshot``).  The next step reads the
+    snapshots whose copies have landed and, at the latest, the one taken two
+    steps earlier (waiting for it if need be, which by then costs nothing),
+    so a timeout in step s raises ``RollfastError`` (``RF_ETIMEOUT``) at the
+    start of step s+1 or s+2: the updates returned by step s and any later
+    step already returned are invalid.  ``check(block=True)`` (used by
+    ``consolidate_momentum`` and ``clear``) waits for every snapshot."""
+
+    DEPTH = 2
+
+    def __init__(self):
+        self.ring = [torch.zeros(2, dtype=torch.int32, pin_memory=True) for _ in range(self.DEPTH + 1)]
+        self.pending = []  # [(slot, event, step, stream)]
+        self.next_slot = 0
+
+    def snapshot(self, stream: torch.cuda.Stream, step: int) -> None:
+        slot = self.next_slot
+        self.next_slot = (slot + 1) % len(self.ring)
+        _lib.error_snapshot(self.ring[slot].data_ptr(), stream.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.pending.append((slot, ev, step, stream))
+
+    def check(self, block: bool = False) -> None:
+        while self.pending:
+            slot, ev, step, stream = self.pending[0]
+            if not (block or len(self.pending) >= self.DEPTH or ev.query()):
+                break
+            ev.synchronize()
+            self.pending.pop(0)
+            words = self.ring[slot].tolist()
+            if words[0] or words[1]:
+                self.pending.clear()
+                try:
+                    _lib.sync_check(stream.cuda_stream)  # reports and clears the words
+                except _lib.RollfastError as exc:
+                    raise _lib.RollfastError(
+                        exc.status, f"sharded Muon step {step}: {exc}; the updates of step {step} and of every "
+                        "later step already returned are invalid") from None
+                raise _lib.RollfastError(_lib.RF_ETIMEOUT, f"sharded Muon step {step}: a bounded device-side "
+                                         f"wait gave up (words {words})")
 
 
 TRANSPORTS = ("auto", "ce", "nccl")
@@ -109,11 +160,14 @@ def use(ctx: ShardContext | None) -> ShardContext | None:
 
 def clear() -> None:
     """Turn sharding off.  Collective when the copy-engine transport has
-    mapped peer buffers: every rank of the group must call it."""
+    mapped peer buffers: every rank of the group must call it.  Raises
+    ``RollfastError`` afterwards if a bounded wait of a sharded step gave up."""
     global _ctx
-    if _ctx is not None:
-        _ctx.close()
-    _ctx = None
+    ctx, _ctx = _ctx, None
+    if ctx is not None:
+        ctx.close()
+        if ctx.errors is not None:
+            ctx.errors.check(block=True)
 
 
 # ---------------------------------------------------------------------------
@@ -254,8 +308,10 @@ def bucket_buffers(plan: ShardPlan, world_size: int, dtype: torch.dtype, device:
 _O_DTYPE = {_lib.RF_NS_F16: torch.float16, _lib.RF_NS_BF16: torch.bfloat16, _lib.RF_NS_F32: torch.float32}
 
 
-def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float):
+def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, decay_f32=None):
     """Sharded version of the fused Muon-branch update (see module doc)."""
+    if decay_f32 is None:
+        decay_f32 = [False] * len(ml)
     from .base import SIDE_CTAS_PER_SM, rf_dtype, run_tail
     from .muon import _finish_leaves, _leaf_table, run_muon_table
     from .peer import PeerGather
@@ -283,6 +339,10 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
         entry = (plan, buffers, gather)
         ctx.plans[key] = entry
     plan, buffers, gather = entry
+    if ctx.errors is None:
+        ctx.errors = ErrorWatch()
+    ctx.errors.check()  # a wait of step s-1 or s-2 that gave up raises here
+    ctx.steps += 1
     ctx.owned_state = [(L.mu_state, plan.owner[i]) for i, L in enumerate(ml)]
     compute = torch.cuda.current_stream(dev)
     # Streams per rank: compute, tail, and either one copy stream (peer.py)
@@ -319,7 +379,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
                 L = ml[i]
                 o = leaf_view(bucket, recv, i, sizes[i])
                 p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
-                items.append((o, p, L.out.view(-1), scales[i], decays[i]))
+                items.append((o, p, L.out.view(-1), scales[i], decays[i], decay_f32[i]))
             run_tail(items, lr, SIDE_CTAS_PER_SM)
             if trace is not None:
                 trace.mark("tail", "tail_end")
@@ -373,7 +433,8 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
                 for i in b.leaves:
                     L = ml[i]
                     p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
-                    items.append((leaf_view(b, recv, i, sizes[i]), p, L.out.view(-1), scales[i], decays[i]))
+                    items.append((leaf_view(b, recv, i, sizes[i]), p, L.out.view(-1), scales[i], decays[i],
+                                  decay_f32[i]))
                 run_tail(items, lr)
         if trace is not None:
             trace.mark("compute", "tail_end")
@@ -384,6 +445,7 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
             done = torch.cuda.Event()
             done.record(side)
             compute.wait_event(done)
+    ctx.errors.snapshot(compute, ctx.steps)
     if trace is not None:
         trace.report(ctx.rank, [sum(sizes[i] for i in b.leaves) for b in plan.buckets])
     return _finish_leaves(ml)
@@ -403,6 +465,8 @@ def consolidate_momentum(ctx: ShardContext | None = None) -> int:
     ctx = ctx or _ctx
     if ctx is None or ctx.world_size == 1:
         return 0
+    if ctx.errors is not None:
+        ctx.errors.check(block=True)  # momentum of a step whose waits gave up is not current anywhere
     for t, owner in ctx.owned_state:
         src = dist.get_global_rank(ctx.group, owner) if ctx.group is not None else owner
         dist.broadcast(t, src=src, group=ctx.group)

@@ -20,7 +20,16 @@ from typing import Any, NamedTuple
 import torch
 
 from . import _lib, _runtime
-from .adam import ScaleByAdamState, adam_seeds, adamw, fresh_key, run_adam, zeros_like_tree
+from .adam import (
+    ScaleByAdamState,
+    adam_seeds,
+    adamw,
+    bump_wd_state,
+    fresh_key,
+    run_adam,
+    wd_count,
+    zeros_like_tree,
+)
 from .base import (
     AddDecayedWeightsState,
     EmptyState,
@@ -32,6 +41,7 @@ from .base import (
     ScaleState,
     add_decayed_weights,
     chain,
+    decay_at,
     has_nonzero_or_scheduled,
     host_count,
     init_empty_state,
@@ -165,7 +175,7 @@ def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str):
     return out
 
 
-def _leaf_table(ml: list, scales, decays):
+def _leaf_table(ml: list, scales, decays, decay_f32=None):
     arr = (_lib.RfMuonLeaf * max(1, len(ml)))()
     for i, L in enumerate(ml):
         b, r, c = L.layout.flat_shape
@@ -183,6 +193,7 @@ def _leaf_table(ml: list, scales, decays):
         e.skip_ns = 0
         e.mu_dtype = rf_dtype(L.mu)
         e.sr_seed = L.seed
+        e.decay_in_f32 = int(bool(decay_f32[i])) if decay_f32 is not None else 0
     return arr
 
 
@@ -231,10 +242,10 @@ def run_muon_table(arr, n: int, prm, dev: torch.device) -> None:
     _lib.check(lib.rf_muon_update(arr, n, ctypes.byref(prm), ws.data_ptr(), ws.numel(), main.cuda_stream))
 
 
-def _run_muon_update(ml, prm, cbuf, scales, decays):
+def _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32=None):
     if not ml:
         return
-    run_muon_table(_leaf_table(ml, scales, decays), len(ml), prm, ml[0].g.device)
+    run_muon_table(_leaf_table(ml, scales, decays, decay_f32), len(ml), prm, ml[0].g.device)
     del cbuf
 
 
@@ -455,10 +466,15 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon")
         ml, muon_key_next = _seed_leaves(ml, muon_st.key)
         scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
-        decays = []
+        # add_decayed_weights of each branch: a constant, or a schedule at the
+        # transform's own count (its state is mstate[0][2] / astate[1]).
+        mwd, mweak = decay_at(weight_decay, wd_count(mstate[0][2])) if muon_wd_on else (0.0, True)
+        awd, aweak = decay_at(eff_adam_wd, wd_count(astate[1])) if adam_wd_on else (0.0, True)
+        decays, decay_f32 = [], []
         for L in ml:
             on = muon_wd_on and bool(masks[L.pos]) and L.p is not None
-            decays.append(round_to_dtype(float(weight_decay), L.p.dtype) if on else 0.0)
+            decays.append((round_to_dtype(mwd, L.p.dtype) if mweak else mwd) if on else 0.0)
+            decay_f32.append(on and not mweak)
         ctx = distributed.current()
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
@@ -466,9 +482,9 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
                                  reserve_sms=ctx.reserve_sms if (ctx is not None and ctx.world_size > 1) else 0,
                                  preconditioning=preconditioning, adaptive=adaptive)
         if ctx is not None and ctx.world_size > 1:
-            outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr)
+            outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32)
         else:
-            _run_muon_update(ml, prm, cbuf, scales, decays)
+            _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32)
             outs = _finish_leaves(ml)
 
         # AdamW fallback leaves.
@@ -486,7 +502,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             out = torch.empty(g.shape, dtype=torch.float32, device=g.device)
             if on:
                 a_items.append((g.contiguous(), amus[i], anus[i], p.contiguous(), out,
-                                round_to_dtype(float(eff_adam_wd), p.dtype), rf_dtype(p)))
+                                round_to_dtype(awd, p.dtype) if aweak else awd,
+                                rf_dtype(p) if aweak else _lib.RF_F32))
             else:
                 a_items.append((g.contiguous(), amus[i], anus[i], None, out, 0.0, _lib.RF_F32))
             a_pos.append(i)
@@ -524,8 +541,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         new_alr = ScaleByScheduleState(safe_increment(alr_state.count)) if callable(
             adam_learning_rate) else alr_state
         new_state = PartitionState({
-            "muon": MaskedState(((new_muon, *mstate[0][1:]), new_mlr)),
-            "adam": MaskedState((new_adam, *astate[1:-1], new_alr)),
+            "muon": MaskedState(((new_muon, *[bump_wd_state(s) for s in mstate[0][1:]]), new_mlr)),
+            "adam": MaskedState((new_adam, *[bump_wd_state(s) for s in astate[1:-1]], new_alr)),
         })
         return tree_unflatten(treedef, full), new_state
 

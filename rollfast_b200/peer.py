@@ -24,7 +24,9 @@ steps identically) and a small flag array per rank
 * after its last tail, a rank stores ``ack[rank] = e`` into every peer.
 
 Waits are bounded device-side polls (``rf_flags_wait``); one that gives up
-raises ``RF_ETIMEOUT`` at the next ``sync_check`` instead of hanging.
+sets a device error word instead of hanging, which the sharded update reads
+back asynchronously after every step (``distributed.ErrorWatch``) and reports
+as ``RF_ETIMEOUT`` one or two steps later.
 
 All pushes go through ONE copy stream, peer after peer in a rotation that
 starts at rank+1 (so every GPU receives from one peer at a time): one stream

@@ -322,3 +322,42 @@ def test_sr_step_seeds_are_deterministic_and_advance_the_key():
     s2, k2 = sr_step_seeds(k1, 5)
     assert not torch.equal(k1, k0) and set(s1).isdisjoint(s2)   # the next step draws new streams
     assert k1.dtype == torch.int64 and k1.shape == (2,) and int(k1.max()) < 2 ** 32
+
+
+def test_decay_typing_follows_jax_promotion():
+    """A Python scalar is weakly typed (product in the parameter dtype); a
+    NumPy scalar or array is strongly typed float32."""
+    from rollfast_b200.base import decay_at
+
+    import oracle as O
+
+    for fn in (decay_at, O.decay_at):
+        assert fn(0.25, 7) == (0.25, True)
+        assert fn(lambda c: 0.1 * c, 3)[1] is True
+        assert fn(lambda c: np.float32(0.1 * c), 3)[1] is False
+        assert fn(lambda c: np.float64(0.5), 0)[1] is False
+        assert fn(lambda c: np.array(0.5, np.float32), 0)[1] is False
+    assert decay_at(lambda c: 0.1 * c, 3)[0] == pytest.approx(0.3)
+
+
+def test_scheduled_decay_states_count_from_zero():
+    params = {"w": torch.zeros(8, 16), "b": torch.zeros(16)}
+    st = rf.muon(learning_rate=0.1, weight_decay=lambda c: 0.01).init(params)
+    assert int(st.inner_states["muon"].inner_state[0][2].count) == 0
+    assert int(st.inner_states["adam"].inner_state[1].count) == 0
+    st_const = rf.muon(learning_rate=0.1, weight_decay=0.01).init(params)
+    assert st_const.inner_states["muon"].inner_state[0][2].count is None
+    st_adamw = rf.adamw(learning_rate=0.1, weight_decay=lambda c: 0.01, weight_decay_mask={"w": True, "b": False})
+    assert int(st_adamw.init(params)[1].inner_state.count) == 0
+
+
+def test_in_transform_decay_oracle_masks_elementwise():
+    import oracle as O
+
+    u = np.array([[1.0, 2.0], [3.0, 4.0]], np.float32)
+    p = np.array([[10.0, 20.0], [30.0, 40.0]], np.float32)
+    m = np.array([[True, False], [False, True]])
+    np.testing.assert_array_equal(O.in_transform_decay(u, p, 0.5, m), [[6.0, 2.0], [3.0, 24.0]])
+    np.testing.assert_array_equal(O.in_transform_decay(u, p, 0.5, np.array([[True, False]])),
+                                  [[6.0, 2.0], [18.0, 4.0]])  # broadcast row mask
+    np.testing.assert_array_equal(O.in_transform_decay(u, p, 0.5, False), u)
