@@ -44,6 +44,7 @@ __all__ = [
     "momentum_runtime",
     "shape_scale_factor",
     "adam_leaf_update",
+    "pow32",
     "decay_at",
     "decay_term",
     "in_transform_decay",
@@ -495,6 +496,16 @@ def apply_updates(p: np.ndarray, u: np.ndarray, param_dtype: str, *, stochastic:
 # --------------------------------------------------------------------------
 
 
+def pow32(b, t: int, dtype=np.float32):
+    """``b ** t`` for a float32 ``b``, correctly rounded to float32 (the power
+    formed in float64).  JAX forms the bias-correction powers (utils.py:505,
+    adam.py:137-141) in float32 with XLA's pow, whose last bit is not pinned;
+    the CUDA host uses this same correctly rounded value.  The last bit
+    matters: 1 - 0.999^t cancels, so one ulp of 0.999^9 is ~7e-6 relative in
+    the AdamW second-moment correction."""
+    return dtype(np.float64(dtype(b)) ** int(t))
+
+
 def momentum_runtime(g: np.ndarray, mu: np.ndarray, count: int, beta: float, *, nesterov: bool,
                      accumulator: str = "ema", dtype=np.float32):
     """utils.py:565-645 as called by scale_by_muon (muon.py:240-253:
@@ -516,8 +527,8 @@ def momentum_runtime(g: np.ndarray, mu: np.ndarray, count: int, beta: float, *, 
     t = count + 1
     if accumulator == "ema":
         k_mu = t + 1 if nesterov else t
-        mu_t = mu_new / (dtype(1.0) - np.power(b, dtype(k_mu), dtype=dtype))
-        g_t = gf / (dtype(1.0) - np.power(b, dtype(t), dtype=dtype)) if nesterov else gf
+        mu_t = mu_new / (dtype(1.0) - pow32(b, k_mu, dtype))
+        g_t = gf / (dtype(1.0) - pow32(b, t, dtype)) if nesterov else gf
     else:
         mu_t = mu_new
         g_t = gf
@@ -586,10 +597,10 @@ def adam_leaf_update(g, mu, nu, count: int, *, b1=0.9, b2=0.999, eps=1e-8, eps_r
     mu_new = ((dtype(1.0) - b1f) * gf + b1f * np.asarray(mu, dtype)).astype(dtype)  # utils.py:437-467
     nu_new = (dtype(1.0 - b2) * np.square(gf) + b2f * np.asarray(nu, dtype)).astype(dtype)  # utils.py:470-493
     t = count + 1
-    mu_bc = dtype(1.0) - np.power(b1f, dtype(t), dtype=dtype)
-    nu_bc = dtype(1.0) - np.power(b2f, dtype(t), dtype=dtype)
+    mu_bc = dtype(1.0) - pow32(b1f, t, dtype)
+    nu_bc = dtype(1.0) - pow32(b2f, t, dtype)
     if nesterov:  # adam.py:140-159
-        mu_bc_next = dtype(1.0) - np.power(b1f, dtype(t + 1), dtype=dtype)
+        mu_bc_next = dtype(1.0) - pow32(b1f, t + 1, dtype)
         mu_hat = b1f * (mu_new / mu_bc_next) + dtype(1.0 - b1) * (gf / mu_bc)
     else:
         mu_hat = mu_new / mu_bc

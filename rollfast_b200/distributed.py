@@ -50,13 +50,14 @@ class ShardContext:
     owned_state: list = field(default_factory=list)  # [(momentum tensor, owner rank)] of the last update
     errors: "ErrorWatch" = None
     steps: int = 0                    # sharded updates run with this context
+    owner_tail: bool = True           # copy-engine transport: owners push final float32 updates
 
     def close(self) -> None:
         """Releases the plans' peer mappings (collective when any exist)."""
         for entry in self.plans.values():
-            gather = entry[2]
-            if gather is not None:
-                gather.close()
+            peer = entry.updates if isinstance(entry, ArenaPlan) else entry[2]
+            if peer is not None:
+                peer.close()
         self.plans.clear()
 
 
@@ -113,13 +114,23 @@ TRANSPORTS = ("auto", "ce", "nccl")
 
 
 def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None = None,
-              transport: str | None = None) -> ShardContext:
+              transport: str | None = None, owner_tail: bool | None = None) -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
 
     ``transport``: how owners' leaves reach the other ranks: ``"ce"`` (copy
     engine pushes into IPC-mapped peer buffers; one host only), ``"nccl"``
     (all-gather), or ``"auto"`` (default; ``ROLLFAST_DIST_GATHER`` overrides):
     ``ce`` when every rank can map its peers' memory, else ``nccl``.
+
+    ``owner_tail`` (copy-engine transport; default on, ``ROLLFAST_DIST_OWNER_TAIL=0``
+    turns it off): each owner computes the final float32 updates of its Muon
+    leaves in the fused epilogue, and the AdamW leaves are split by element
+    range, so no rank runs a tail or AdamW over data it does not own; the
+    copy engines push the updates into every peer's update arena, and the
+    returned update tensors are views of that arena, valid until the next
+    update is queued on the caller's stream (``peer.PeerUpdates``).  Off: the
+    owners exchange 16-bit O and every rank runs the tail over all leaves
+    into fresh buffers.
 
     ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
     all-gather (NCCL) runs beside it without displacing GEMM CTAs; default:
@@ -131,6 +142,8 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
         buckets = int(os.environ.get("ROLLFAST_DIST_BUCKETS", "4") or 4)
     if transport is None:
         transport = os.environ.get("ROLLFAST_DIST_GATHER", "auto") or "auto"
+    if owner_tail is None:
+        owner_tail = os.environ.get("ROLLFAST_DIST_OWNER_TAIL", "1") != "0"
     transport = transport.lower()
     if transport not in TRANSPORTS:
         raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
@@ -142,7 +155,8 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
     if _ctx is not None:
         _ctx.close()
     _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
-                        buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)), transport=transport)
+                        buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)), transport=transport,
+                        owner_tail=bool(owner_tail))
     return _ctx
 
 
@@ -451,6 +465,120 @@ def sharded_muon_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: fl
     return _finish_leaves(ml)
 
 
+@dataclass
+class ArenaPlan:
+    """Ownership, arena layout and the mapped arena of one sharded tree
+    (owner-side tail)."""
+
+    plan: ShardPlan                   # Muon leaf owners and buckets
+    updates: object                   # peer.PeerUpdates
+    muon_offsets: list                # arena offset of each Muon leaf
+    adam_offsets: list                # arena offset of each AdamW leaf
+    adam_spans: list                  # [(start, end)] of the AdamW region per owner rank
+    adam_region: int                  # region index of the AdamW leaves
+
+
+def _arena_plan(ctx: ShardContext, ml, a_items, prm, dev):
+    from .peer import PeerUpdates, arena_layout, split_range
+
+    sizes = [L.out.numel() for L in ml]
+    steps = prm.n_coeff_rows or prm.ns_steps
+    costs = [ns_flops(*L.layout.flat_shape) * steps for L in ml]
+    plan = make_plan(sizes, costs, ctx.world_size, ctx.buckets) if ml else ShardPlan([], [], [0] * ctx.world_size)
+    regions = [[(i, plan.owner[i], sizes[i]) for i in b.leaves] for b in plan.buckets]
+    offs, ranges, total = arena_layout(regions, ctx.world_size)
+    muon_offsets = [offs[i] for i in range(len(ml))]
+    # AdamW leaves: laid out one after another and split by element count.
+    adam_offsets, acc = [], total
+    for it in a_items:
+        adam_offsets.append(acc)
+        acc += (it[0].numel() + 63) // 64 * 64
+    adam_region = len(ranges)
+    adam_spans = split_range(total, acc - total, ctx.world_size)
+    if a_items:
+        ranges.append(adam_spans)
+    updates = PeerUpdates.create(ranges, max(acc, 1), ctx, dev, required=ctx.transport == "ce")
+    if updates is None:
+        return None
+    return ArenaPlan(plan, updates, muon_offsets, adam_offsets, adam_spans, adam_region)
+
+
+def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, decay_f32, a_items, adam_kw,
+                   a_seeds=None):
+    """Sharded Muon branch + AdamW leaves with the owner-side tail (copy-engine
+    transport).  Returns ``(muon_outs, adam_outs)`` in the order of ``ml`` and
+    ``a_items``, or None when the peers cannot be mapped (the caller then
+    takes the gathered-O path).
+
+    Per step: every rank signals that its stream reached the step; it runs
+    AdamW on its element range of the AdamW leaves and momentum + Newton-Schulz
+    with the fused tail on the Muon leaves it owns, bucket by bucket, each
+    writing final float32 updates into its arena; after each piece the copy
+    engines push the owner's span to every peer; the step ends when every
+    owner's pushes have landed."""
+    from .adam import run_adam
+    from .base import rf_dtype
+    from .muon import _finish_leaves, _leaf_table, run_muon_table
+
+    dev = (ml[0].g if ml else a_items[0][0]).device
+    key = ("arena", tuple((L.layout.flat_shape, L.g.dtype) for L in ml),
+           tuple((tuple(it[0].shape), it[0].dtype) for it in a_items), prm.n_coeff_rows or prm.ns_steps, dev)
+    entry = ctx.plans.get(key)
+    if entry is None:
+        entry = _arena_plan(ctx, ml, a_items, prm, dev)
+        if entry is None:
+            return None
+        ctx.plans[key] = entry
+    if ctx.errors is None:
+        ctx.errors = ErrorWatch()
+    ctx.errors.check()  # a wait of step s-1 or s-2 that gave up raises here
+    ctx.steps += 1
+    plan, up = entry.plan, entry.updates
+    arena = up.arena
+    compute = torch.cuda.current_stream(dev)
+    ml = [L._replace(out=arena[o: o + L.out.numel()].view(L.out.shape)) for L, o in zip(ml, entry.muon_offsets)]
+    a_outs = [arena[o: o + it[0].numel()].view(it[0].shape) for it, o in zip(a_items, entry.adam_offsets)]
+    owned = [(L.mu_state, plan.owner[i]) for i, L in enumerate(ml)]
+
+    up.begin_step(compute)
+    # AdamW first: its push overlaps the first bucket's Newton-Schulz.
+    if a_items:
+        mine, seeds = [], []
+        for j, (it, o, out) in enumerate(zip(a_items, entry.adam_offsets, a_outs)):
+            g, mu, nu, p = it[0], it[1], it[2], it[3]
+            n = g.numel()
+            for r, (slo, shi) in enumerate(entry.adam_spans):
+                a, b = max(slo - o, 0), min(shi - o, n)
+                if a >= b:
+                    continue
+                owned += [(mu.view(-1)[a:b], r), (nu.view(-1)[a:b], r)]
+                if r == ctx.rank:
+                    mine.append((g.view(-1)[a:b], mu.view(-1)[a:b], nu.view(-1)[a:b],
+                                 None if p is None else p.reshape(-1)[a:b], out.view(-1)[a:b], *it[5:7]))
+                    if a_seeds is not None:  # a slice keeps its leaf's noise streams
+                        seeds += [a_seeds[2 * j], a_seeds[2 * j + 1]]
+        run_adam(mine, seeds=seeds if a_seeds is not None else None, **adam_kw)
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        up.push(entry.adam_region, ev)
+    for b in plan.buckets:
+        ids = [i for i in b.leaves if plan.owner[i] == ctx.rank]
+        if ids:
+            sub = [ml[i] for i in ids]
+            arr = _leaf_table(sub, [scales[i] for i in ids], [decays[i] for i in ids],
+                              [decay_f32[i] for i in ids])
+            for j in range(len(ids)):
+                arr[j].out_dtype = rf_dtype(sub[j].out)
+            run_muon_table(arr, len(ids), prm, dev)
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        up.push(b.index, ev)
+    up.finish(compute)
+    ctx.owned_state = owned
+    ctx.errors.snapshot(compute, ctx.steps)
+    return _finish_leaves(ml), a_outs
+
+
 def consolidate_momentum(ctx: ShardContext | None = None) -> int:
     """Make the Muon momentum current on every rank (collective over the
     group), e.g. before saving a checkpoint from one rank.
@@ -474,12 +602,13 @@ def consolidate_momentum(ctx: ShardContext | None = None) -> int:
 
 
 def active_transport(ctx: ShardContext | None = None) -> str:
-    """The transport the context's plans use: "ce", "nccl", or the configured
-    value when no plan has been built yet."""
+    """The transport the context's plans use: "ce+owner_tail", "ce",
+    "nccl", or the configured value when no plan has been built yet."""
     ctx = ctx or _ctx
     if ctx is None:
         return "none"
-    kinds = {("ce" if e[2] is not None else "nccl") for e in ctx.plans.values()}
+    kinds = {("ce+owner_tail" if isinstance(e, ArenaPlan) else ("ce" if e[2] is not None else "nccl"))
+             for e in ctx.plans.values()}
     return kinds.pop() if len(kinds) == 1 else ctx.transport
 
 

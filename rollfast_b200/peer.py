@@ -209,3 +209,187 @@ class PeerGather:
             ev = torch.cuda.Event()
             ev.record(s)
             compute.wait_event(ev)
+
+
+# ---------------------------------------------------------------------------
+# Owner-side tail: a float32 update arena pushed by its owners.
+# ---------------------------------------------------------------------------
+
+
+def arena_layout(regions, world_size: int, align: int = 64):
+    """Element layout of the update arena.
+
+    ``regions``: one list per exchange region (the Muon buckets) of
+    ``(key, owner, numel)`` leaves.  Within a region the leaves are grouped
+    by owner (in rank order, leaf order kept within an owner), so each
+    owner's leaves form one contiguous span; every leaf starts
+    ``align``-element aligned (vector epilogue stores).  Returns
+    ``(offsets, ranges, total)``: ``offsets[key]`` a leaf's element offset,
+    ``ranges[k][r] = (start, end)`` owner r's span of region k, ``total``
+    the elements laid out."""
+    acc = 0
+    offsets, ranges = {}, []
+    for leaves in regions:
+        span = []
+        for owner in range(world_size):
+            start = acc
+            for key, o, n in leaves:
+                if o == owner:
+                    offsets[key] = acc
+                    acc += (n + align - 1) // align * align
+            span.append((start, acc))
+        ranges.append(span)
+    return offsets, ranges, acc
+
+
+def split_range(start: int, total: int, world_size: int, align: int = 64):
+    """``world_size`` contiguous spans covering ``[start, start + total)``,
+    boundaries ``align``-element aligned, as equal as the alignment allows."""
+    units = (total + align - 1) // align
+    spans, lo = [], start
+    for r in range(world_size):
+        hi = start + min(total, (units * (r + 1) // world_size) * align)
+        spans.append((lo, hi))
+        lo = hi
+    return spans
+
+
+def _map_peer_buffers(ctx, tensors, required: bool):
+    """Collective: exports ``tensors`` (device buffers) and maps every peer's
+    counterparts.  Returns ``(remote, mapped, why)``: ``remote[r]`` the list of
+    rank r's buffer addresses in this process (None for this rank),
+    ``mapped`` the bases to close, ``why`` None on success on every rank."""
+    import torch.distributed as dist
+
+    try:
+        exported = [_lib.ipc_export(t.data_ptr()) for t in tensors]
+        mine = (True, socket.gethostname(), exported)
+    except Exception as exc:  # noqa: BLE001 - reported to every rank below
+        mine = (False, repr(exc), None)
+    infos = [None] * ctx.world_size
+    dist.all_gather_object(infos, mine, group=ctx.group)
+    why = next((f"rank {r}: {i[1]}" for r, i in enumerate(infos) if not i[0]), None)
+    if why is None and len({i[1] for i in infos}) != 1:
+        why = "ranks are on more than one host"
+    remote, mapped = [None] * ctx.world_size, []
+    if why is None:
+        try:
+            for r, info in enumerate(infos):
+                if r == ctx.rank:
+                    continue
+                addrs = []
+                for handle, off in info[2]:
+                    base = _lib.ipc_open(handle)
+                    mapped.append(base)
+                    addrs.append(base + off)
+                remote[r] = addrs
+        except Exception as exc:  # noqa: BLE001
+            why = f"rank {ctx.rank}: {exc!r}"
+    oks = [None] * ctx.world_size
+    dist.all_gather_object(oks, why, group=ctx.group)
+    failed = next((w for w in oks if w is not None), None)
+    if failed is not None:
+        for base in mapped:
+            _lib.ipc_close(base)
+        if required:
+            raise RuntimeError(f"copy-engine exchange unavailable: {failed}")
+        return None, [], failed
+    return remote, mapped, None
+
+
+class PeerUpdates:
+    """The float32 update arena of one ownership plan, mapped by every peer.
+
+    Each rank holds the whole sharded update tree in one flat float32 buffer
+    (``arena_layout``).  An owner's fused Newton-Schulz epilogue (and its
+    AdamW slice) writes the final updates ``-lr (shape O + decay p)`` of its
+    leaves straight into its own arena; the copy engines then push each
+    owner's span of a region into the same span of every peer's arena.  No
+    rank runs a tail over leaves it does not own, and the update tensors the
+    step returns are views of the arena.
+
+    Ordering, with epoch ``e`` per step and flags ``arrive[region][sender]``
+    then ``ready[sender]``:
+
+    * at the start of step e each rank stores ``ready[rank] = e`` into every
+      peer, on its compute stream, i.e. after whatever the caller queued
+      before the step (applying step e-1's updates, which are overwritten
+      now);
+    * an owner's first push of step e waits until every peer's ``ready >= e``;
+    * after pushing region k an owner stores ``arrive[k][owner] = e`` into
+      every rank (itself included);
+    * the step ends with the compute stream waiting for ``arrive[*][*] >= e``
+      and for this rank's own pushes.
+
+    Updates returned by step e therefore stay valid until the next update is
+    queued on the caller's stream."""
+
+    def __init__(self, ranges, total, rank, world_size, group, device, timeout_s=None):
+        self.ranges, self.rank, self.world, self.group = ranges, rank, world_size, group
+        self.device = device
+        self.timeout_s = default_timeout_s() if timeout_s is None else float(timeout_s)
+        self.arena = torch.empty(total, dtype=torch.float32, device=device)
+        self.n_regions = len(ranges)
+        if self.n_regions * world_size > 64:
+            raise ValueError("too many exchange regions for one flag wait (regions x ranks must be <= 64)")
+        self.flags = torch.zeros(self.n_regions * world_size + world_size, dtype=torch.int32, device=device)
+        self.epoch = 0
+        self.remote = [None] * world_size
+        self._mapped: list[int] = []
+        self.copy_stream = torch.cuda.Stream(device=device)
+
+    @classmethod
+    def create(cls, ranges, total, ctx, device, *, required: bool):
+        g = cls(ranges, total, ctx.rank, ctx.world_size, ctx.group, device)
+        torch.cuda.synchronize(device)  # flags are zero before any peer can signal
+        remote, mapped, why = _map_peer_buffers(ctx, [g.arena, g.flags], required)
+        if why is not None:
+            return None
+        g.remote, g._mapped = remote, mapped
+        return g
+
+    def close(self, barrier: bool = True) -> None:
+        if barrier:
+            import torch.distributed as dist
+
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+        for base in self._mapped:
+            _lib.ipc_close(base)
+        self._mapped = []
+        self.remote = [None] * self.world
+
+    def _peers(self):
+        return [(self.rank + 1 + j) % self.world for j in range(self.world - 1)]
+
+    def _flag_addr(self, r: int, index: int) -> int:
+        base = self.flags.data_ptr() if r == self.rank else self.remote[r][1]
+        return base + 4 * index
+
+    def begin_step(self, compute: torch.cuda.Stream) -> None:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        ready = self.n_regions * self.world + self.rank
+        _lib.flags_signal([self._flag_addr(r, ready) for r in self._peers()], self.epoch, compute.cuda_stream)
+        readys = self.flags.data_ptr() + 4 * self.n_regions * self.world
+        _lib.flags_wait(readys, self.world, self.rank, self.epoch, self.timeout_s, self.copy_stream.cuda_stream)
+
+    def push(self, k: int, ready: torch.cuda.Event) -> None:
+        """Push this rank's span of region ``k`` (complete at ``ready``)."""
+        start, end = self.ranges[k][self.rank]
+        s = self.copy_stream
+        s.wait_event(ready)
+        nbytes = (end - start) * 4
+        if nbytes:
+            src = self.arena.data_ptr() + start * 4
+            for r in self._peers():
+                _lib.peer_copy(self.remote[r][0] + start * 4, src, nbytes, s.cuda_stream)
+        idx = k * self.world + self.rank
+        _lib.flags_signal([self._flag_addr(r, idx) for r in range(self.world)], self.epoch, s.cuda_stream)
+
+    def finish(self, compute: torch.cuda.Stream) -> None:
+        """Order ``compute`` after every owner's pushes of this step."""
+        _lib.flags_wait(self.flags.data_ptr(), self.n_regions * self.world, -1, self.epoch, self.timeout_s,
+                        compute.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(self.copy_stream)
+        compute.wait_event(ev)

@@ -42,8 +42,8 @@ def _f32_ns():
 
 
 SCHEDULES = {
-    "python_float": lambda c: 0.5 * (c + 1),            # weakly typed
-    "float32_array": lambda c: np.float32(0.5 * (c + 1)),  # strongly typed
+    "python_float": lambda c: 0.3 + 0.1 * c,                # weakly typed
+    "float32_array": lambda c: np.float32(0.3 + 0.1 * c),   # strongly typed
 }
 
 

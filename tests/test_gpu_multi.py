@@ -1,7 +1,10 @@
-"""Sharded Muon on 2 GPUs: leaf ownership + all-gather (copy-engine pushes
-into IPC-mapped peer buffers, and NCCL) must give the same updates as the
-unsharded single-GPU path, step after step.  Runs as child processes and
-needs >= 2 GPUs (skipped otherwise)."""
+"""Sharded Muon on 2 GPUs: leaf ownership + exchange must give the same
+updates as the unsharded single-GPU path, step after step, for every
+transport: the owner-side tail (owners push final float32 updates into the
+peers' IPC-mapped update arenas; AdamW split by element range: bit-identical
+to the unsharded run), and the gathered-O forms (copy-engine pushes of 16-bit
+O, or an NCCL all-gather, then a tail on every rank: within 2e-3).  Runs as
+child processes and needs >= 2 GPUs (skipped otherwise)."""
 
 import os
 import socket
@@ -26,7 +29,7 @@ def _tree(dev, seed):
     return {k: torch.randn(s, device=dev, generator=g).to(torch.bfloat16) for k, s in shapes.items()}
 
 
-def _worker(rank, world, port, transport, q):
+def _worker(rank, world, port, transport, owner_tail, q):
     import datetime
 
     import torch.distributed as dist
@@ -37,6 +40,9 @@ def _worker(rank, world, port, transport, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    # One tensor-core kernel for every group size, so the sharded run (fewer
+    # matrices per launch) and the unsharded one execute the same kernel.
+    os.environ["ROLLFAST_NS_KERNEL"] = "2"
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -51,21 +57,25 @@ def _worker(rank, world, port, transport, q):
         ok = True
         # One sharded context over three steps (the copy-engine epochs and
         # acknowledgements advance), then a fresh context (mappings rebuilt).
-        ctx = rf.distributed.configure(buckets=2, transport=transport)
+        ctx = rf.distributed.configure(buckets=2, transport=transport, owner_tail=owner_tail)
+        expect = "ce+owner_tail" if (transport == "ce" and owner_tail) else transport
         for step in range(4):
             grads = _tree(dev, 10 + step)
             if step == 3:
                 rf.distributed.clear()
-                ctx = rf.distributed.configure(buckets=3, transport=transport)
+                ctx = rf.distributed.configure(buckets=3, transport=transport, owner_tail=owner_tail)
             rf.distributed.use(None)                 # reference: the unsharded path
             u_ref, ref_st = ref_tx.update(grads, ref_st, params)
             rf.distributed.use(ctx)
             u_sh, sh_st = sh_tx.update(grads, sh_st, params)
             _lib.sync_check(torch.cuda.current_stream().cuda_stream)  # no flag wait gave up
-            ok &= rf.distributed.active_transport(ctx) == transport
+            ok &= rf.distributed.active_transport(ctx) == expect
             for k in params:
-                e = float(torch.linalg.vector_norm(u_sh[k] - u_ref[k]) / torch.linalg.vector_norm(u_ref[k]))
-                ok &= e <= 2e-3  # 16-bit gathered O vs fused fp32 O
+                if expect == "ce+owner_tail":
+                    ok &= bool(torch.equal(u_sh[k], u_ref[k]))  # same kernels, same fused epilogue
+                else:
+                    e = float(torch.linalg.vector_norm(u_sh[k] - u_ref[k]) / torch.linalg.vector_norm(u_ref[k]))
+                    ok &= e <= 2e-3  # 16-bit gathered O vs fused fp32 O
         # Momentum is current only on each leaf's owner until consolidated;
         # then it equals the unsharded run's, bit for bit.
         rf.distributed.consolidate_momentum(ctx)
@@ -74,6 +84,10 @@ def _worker(rank, world, port, transport, q):
         for k, v in params.items():
             if v.ndim >= 2:
                 ok &= bool(torch.equal(mu_sh[k], mu_ref[k]))
+        # AdamW moments: split by element range under the owner-side tail,
+        # replicated otherwise; consolidated, they equal the unsharded run's.
+        a_sh, a_ref = sh_st.inner_states["adam"].inner_state[0], ref_st.inner_states["adam"].inner_state[0]
+        ok &= bool(torch.equal(a_sh.mu["norm"], a_ref.mu["norm"])) and bool(torch.equal(a_sh.nu["norm"], a_ref.nu["norm"]))
         rf.distributed.clear()
         q.put((rank, ok))
     except Exception as exc:  # report instead of hanging the other rank
@@ -82,8 +96,8 @@ def _worker(rank, world, port, transport, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["ce", "nccl"])
-def test_sharded_update_matches_single_gpu_on_two_gpus(transport):
+@pytest.mark.parametrize("transport,owner_tail", [("ce", True), ("ce", False), ("nccl", False)])
+def test_sharded_update_matches_single_gpu_on_two_gpus(transport, owner_tail):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -91,7 +105,7 @@ def test_sharded_update_matches_single_gpu_on_two_gpus(transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, transport, owner_tail, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in procs)
