@@ -543,168 +543,6 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         full = list(leaves)
         for L, o in zip(ml, outs):
             full[L.pos] = o
-        new_state = MuonState(safe_increment(state.count), state.mu, state.ns_coeffs, state.magma_s, key_next)
-        return tree_unflatten(treedef, full), new_state
-
-    return GradientTransformation(init_fn, update_fn)
-
-
-def _build_unscaled_muon_branch(*, ns_coeffs, ns_steps, beta, eps, mu_dtype, nesterov, adaptive, preconditioning,
-                                weight_dimension_numbers, orthogonalize_fn, momentum_accumulator, use_magma,
-                                magma_p, magma_tau, consistent_rms, weight_decay, weight_decay_mask, axis_name,
-                                key) -> GradientTransformation:
-    """muon.py:335-395."""
-    components = [
-        scale_by_muon(ns_coeffs=ns_coeffs, ns_steps=ns_steps, beta=beta, eps=eps, mu_dtype=mu_dtype,
-                      nesterov=nesterov, adaptive=adaptive, preconditioning=preconditioning,
-                      weight_dimension_numbers=weight_dimension_numbers, orthogonalize_fn=orthogonalize_fn,
-                      momentum_accumulator=momentum_accumulator, use_magma=use_magma, magma_p=magma_p,
-                      magma_tau=magma_tau, shape_updates=use_magma, consistent_rms=consistent_rms,
-                      weight_decay=weight_decay if use_magma else 0.0,
-                      weight_decay_mask=weight_decay_mask if use_magma else None, axis_name=axis_name, key=key)
-    ]
-    if not use_magma:
-        components.append(scale_by_shape(weight_dimension_numbers=weight_dimension_numbers,
-                                         consistent_rms=consistent_rms))
-        if has_nonzero_or_scheduled(weight_decay):
-            components.append(add_decayed_weights(weight_decay, weight_decay_mask))
-    return chain(*components)
-
-
-def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8, weight_decay=0.0,
-         weight_decay_mask=None, mu_dtype=None, *, nesterov: bool = True, adaptive: bool = False,
-         preconditioning: str = "frobenius", adam_b1=0.9, adam_b2=0.999, adam_eps=None, adam_eps_root=0.0,
-         adam_weight_decay=None, adam_learning_rate=None, muon_weight_dimension_numbers=None,
-         consistent_rms=None, orthogonalize_fn=orthogonalize_via_newton_schulz,
-         momentum_accumulator: str = "ema", use_magma: bool = False, magma_p: float = 0.5,
-         magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
-    """muon.py:398-486: Muon with automatic Muon/AdamW partitioning."""
-    if adam_learning_rate is None:
-        adam_learning_rate = learning_rate
-    if adam_eps is None:
-        adam_eps = eps
-    eff_adam_wd = weight_decay if adam_weight_decay is None else adam_weight_decay
-    part = _make_matrix_partition_fns(muon_weight_dimension_numbers, "muon")
-    branch = _build_unscaled_muon_branch(
-        ns_coeffs=ns_coeffs, ns_steps=ns_steps, beta=beta, eps=eps, mu_dtype=mu_dtype, nesterov=nesterov,
-        adaptive=adaptive, preconditioning=preconditioning, weight_dimension_numbers=part.masked_specs,
-        orthogonalize_fn=orthogonalize_fn, momentum_accumulator=momentum_accumulator, use_magma=use_magma,
-        magma_p=magma_p, magma_tau=magma_tau, consistent_rms=consistent_rms, weight_decay=weight_decay,
-        weight_decay_mask=weight_decay_mask, axis_name=axis_name, key=key)
-    adam_tx = adamw(learning_rate=adam_learning_rate, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
-                    weight_decay=eff_adam_wd, weight_decay_mask=weight_decay_mask, mu_dtype=mu_dtype,
-                    nesterov=nesterov, use_magma=use_magma, magma_p=magma_p, magma_tau=magma_tau,
-                    axis_name=axis_name, key=key)
-    composite = partition({"muon": chain(branch, scale_by_learning_rate(learning_rate)), "adam": adam_tx},
-                          part.labels)
-    if orthogonalize_fn is not orthogonalize_via_newton_schulz:
-        return composite  # custom hook: run the chain transform by transform
-
-    muon_wd_on = has_nonzero_or_scheduled(weight_decay)
-    adam_wd_on = has_nonzero_or_scheduled(eff_adam_wd)
-
-    def fused_update(updates, state, params=None):
-        from . import distributed  # late import: optional torch.distributed plumbing
-
-        if params is None:
-            # scale_by_muon resolves the callable partition specs from params
-            # (dimension_numbers.py:127-132).
-            raise ValueError(
-                "`params` must be provided to `scale_by_muon` when `weight_dimension_numbers` is callable."
-            )
-        labels = part.labels(updates)
-        specs_tree = part.masked_specs(params)
-        leaves, treedef = tree_flatten(updates, is_leaf=is_aux_leaf)
-        lab = tree_flatten(labels, is_leaf=lambda x: x is None or isinstance(x, str))[0]
-        specs = _flatten_specs(specs_tree, len(leaves))
-        ps = tree_flatten(params, is_leaf=is_aux_leaf)[0]
-        mask_tree = resolve_mask(weight_decay_mask, params)
-        masks = tree_flatten(mask_tree, is_leaf=is_aux_leaf)[0] if mask_tree is not None else [True] * len(leaves)
-
-        mstate = state.inner_states["muon"].inner_state  # ((MuonState, Empty, [wd]), lr_state)
-        astate = state.inner_states["adam"].inner_state  # (ScaleByAdamState, [wd], lr_state)
-        muon_st: MuonState = mstate[0][0]
-        mlr_state = mstate[1]
-        adam_st: ScaleByAdamState = astate[0]
-        alr_state = astate[-1]
-        lr = resolve_scalar(learning_rate, host_count(mlr_state.count)) if callable(learning_rate) else float(
-            learning_rate)
-        alr = resolve_scalar(adam_learning_rate, host_count(alr_state.count)) if callable(
-            adam_learning_rate) else float(adam_learning_rate)
-
-        mus = tree_flatten(muon_st.mu, is_leaf=is_aux_leaf)[0]
-        muon_leaves = [g if (not is_aux_leaf(g) and l == "muon") else None for g, l in zip(leaves, lab)]
-        muon_specs = [s if l == "muon" else None for s, l in zip(specs, lab)]
-        for g, s in zip(muon_leaves, muon_specs):
-            if g is not None:
-                _validate_matrix_operand(g, s, "scale_by_muon")
-        ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon")
-        ml, muon_key_next = _seed_leaves(ml, muon_st.key)
-        scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
-        # add_decayed_weights of each branch: a constant, or a schedule at the
-        # transform's own count (its state is mstate[0][2] / astate[1]).
-        mwd, mweak = decay_at(weight_decay, wd_count(mstate[0][2])) if muon_wd_on else (0.0, True)
-        awd, aweak = decay_at(eff_adam_wd, wd_count(astate[1])) if adam_wd_on else (0.0, True)
-        decays, decay_f32 = [], []
-        for L in ml:
-            on = muon_wd_on and bool(masks[L.pos]) and L.p is not None
-            decays.append((round_to_dtype(mwd, L.p.dtype) if mweak else mwd) if on else 0.0)
-            decay_f32.append(on and not mweak)
-        ctx = distributed.current()
-        prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
-                                 accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
-                                 ns_steps=ns_steps, lr=lr, fuse_tail=1,
-                                 reserve_sms=ctx.reserve_sms if (ctx is not None and ctx.world_size > 1) else 0,
-                                 preconditioning=preconditioning, adaptive=adaptive)
-        if ctx is not None and ctx.world_size > 1:
-            outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32)
-        else:
-            _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32)
-            outs = _finish_leaves(ml)
-
-        # AdamW fallback leaves.
-        a_items, a_pos = [], []
-        amus = tree_flatten(adam_st.mu, is_leaf=is_aux_leaf)[0]
-        anus = tree_flatten(adam_st.nu, is_leaf=is_aux_leaf)[0]
-        for i, (g, l) in enumerate(zip(leaves, lab)):
-            if is_aux_leaf(g) or l != "adam":
-                continue
-            require_cuda(g, "gradient")
-            if g.dtype.is_complex:
-                raise NotImplementedError("complex leaves are not on the B200 hot path")
-            p = ps[i]
-            on = adam_wd_on and bool(masks[i]) and p is not None and not is_aux_leaf(p)
-            out = torch.empty(g.shape, dtype=torch.float32, device=g.device)
-            if on:
-                a_items.append((g.contiguous(), amus[i], anus[i], p.contiguous(), out,
-                                round_to_dtype(awd, p.dtype) if aweak else awd,
-                                rf_dtype(p) if aweak else _lib.RF_F32))
-            else:
-                a_items.append((g.contiguous(), amus[i], anus[i], None, out, 0.0, _lib.RF_F32))
-            a_pos.append(i)
-        a_seeds, adam_key_next = adam_seeds(a_items, adam_st.key)
-        if a_items:
-            # The fallback leaves are independent of the Muon branch: with
-            # pipelining they run on the aux stream, beside the last GEMMs.
-            dev = a_items[0][0].device
-            main = torch.cuda.current_stream(dev)
-            side = _runtime.aux_stream(dev) if _runtime.pipelined() else main
-            if side is not main:
-                side.wait_stream(main)
-            with torch.cuda.stream(side):
-                run_adam(a_items, b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
-                         count=host_count(adam_st.count), nesterov=nesterov, lr=alr,
-                         max_ctas_per_sm=SIDE_CTAS_PER_SM if side is not main else 0, seeds=a_seeds)
-            if side is not main:
-                main.wait_stream(side)
-                for it in a_items:
-                    for t in it[:5]:
-                        if t is not None:
-                            t.record_stream(side)
-
-        full = list(leaves)
-        for L, o in zip(ml, outs):
-            full[L.pos] = o
         for i, o in zip(a_pos, a_outs):
             full[i] = o
 
