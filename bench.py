@@ -79,16 +79,25 @@ def llama3_8b_shapes(layers: int = 32, vocab: int = 128256):
             "embed": (vocab, 4096), "unembed": (vocab, 4096)}
 
 
-def muon_specs(shapes, rf):
+def llama3_70b_shapes(layers: int = 80):
+    """80 layers, hidden 8192, 64 query heads of 128
+    (8192x8192 q, o), 8 KV heads (8192x1024 k, v), 8192x28672 gate / up,
+    28672x8192 down; RMSNorm vectors to AdamW (no embedding in the config)."""
+    layer = {"q": (8192, 8192), "k": (8192, 1024), "v": (8192, 1024), "o": (8192, 8192),
+             "gate": (8192, 28672), "up": (8192, 28672), "down": (28672, 8192),
+             "attn_norm": (8192,), "mlp_norm": (8192,)}
+    return {"layers": [dict(layer) for _ in range(layers)], "final_norm": (8192,)}
+
+
+def muon_specs(shapes, rf, name=None):
     """2-D weight matrices -> Muon; vectors, embed and unembed -> AdamW."""
-    def spec(path_leaf_name, s):
-        if len(s) == 2 and path_leaf_name not in ("embed", "unembed"):
-            return rf.MatrixDimensionNumbers()
-        return None
-    return {
-        "layers": [{k: spec(k, s) for k, s in layer.items()} for layer in shapes["layers"]],
-        "final_norm": None, "embed": None, "unembed": None,
-    }
+    if isinstance(shapes, dict):
+        return {k: muon_specs(v, rf, k) for k, v in shapes.items()}
+    if isinstance(shapes, list):
+        return [muon_specs(v, rf, name) for v in shapes]
+    if len(shapes) == 2 and name not in ("embed", "unembed"):
+        return rf.MatrixDimensionNumbers()
+    return None
 
 
 def map_shapes(shapes, fn):
@@ -123,6 +132,14 @@ def ns_alg_flops(shapes, steps=5):
 
 def muon_matrix_shapes(shapes):
     return [s for layer in shapes["layers"] for k, s in layer.items() if len(s) == 2]
+
+
+WORKLOADS = {
+    # name: (shapes fn, muon kwargs, BASELINE config)
+    "llama3_8b_muon_step": (llama3_8b_shapes, {}, "configs[2]"),
+    "llama3_70b_muon_step": (llama3_70b_shapes, {"momentum_accumulator": "heavy_ball", "nesterov": False},
+                             "configs[4]"),
+}
 
 
 # ---------------------------------------------------------------------------
@@ -308,32 +325,38 @@ def run_reference(args, rank, world):
 
 PARITY_SHAPES = {"q": (4096, 4096), "k": (4096, 1024), "gate": (4096, 14336), "down": (14336, 4096),
                  "norm": (4096,)}
+# Llama-3-70B: the q and k/v shapes (the 8192x28672 leaves would take the
+# oracle minutes on the host).
+PARITY_SHAPES_70B = {"q": (8192, 8192), "k": (8192, 1024), "norm": (8192,)}
 PARITY_TOL = {"muon": 1e-2, "adamw": 1e-6, "sharded": 1e-2}
 
 
-def parity_check(rf, dev, dist, rank: int, world: int) -> dict:
+def parity_check(rf, dev, dist, rank: int, world: int, shapes=None, muon_kw=None) -> dict:
     """One fresh step (lr 0.02, wd 0.01, beta 0.95, 5 standard iterations) of
-    a tree with the four Llama-3-8B matrix shapes and one AdamW vector, run
-    after the timed region.  Rank 0 compares the updates with the oracle
-    (NumPy float32) on the same inputs; on more than one GPU every rank runs
-    the sharded update and rank 0 also recomputes it unsharded."""
+    a tree with the workload's matrix shapes and one AdamW vector, run after
+    the timed region.  Rank 0 compares the updates with the oracle (NumPy
+    float32) on the same inputs; on more than one GPU every rank runs the
+    sharded update (in the workload's mode) and rank 0 also recomputes it
+    unsharded and compares the leaves it holds."""
+    shapes = PARITY_SHAPES if shapes is None else shapes
+    muon_kw = muon_kw or {}
     rng = np.random.default_rng(4321)
     import oracle as O
 
-    p_np = {k: O.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32)) for k, s in PARITY_SHAPES.items()}
-    g_np = {k: O.bf16_round(rng.standard_normal(s).astype(np.float32)) for k, s in PARITY_SHAPES.items()}
+    p_np = {k: O.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32)) for k, s in shapes.items()}
+    g_np = {k: O.bf16_round(rng.standard_normal(s).astype(np.float32)) for k, s in shapes.items()}
     to = lambda a: torch.from_numpy(a).to(dev).to(torch.bfloat16)  # noqa: E731
     params = {k: to(v) for k, v in p_np.items()}
     grads = {k: to(v) for k, v in g_np.items()}
 
     def step():
-        tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95)
+        tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95, **muon_kw)
         u, _ = tx.update(grads, tx.init(params), params)
         torch.cuda.synchronize()
-        return {k: v.float().cpu().numpy() for k, v in u.items()}
+        return {k: (None if v.is_meta else v.float().cpu().numpy()) for k, v in u.items()}
 
     got = step()
-    out = {"leaves": {k: list(s) for k, s in PARITY_SHAPES.items()}, "tol": dict(PARITY_TOL),
+    out = {"leaves": {k: list(s) for k, s in shapes.items()}, "tol": dict(PARITY_TOL), "options": dict(muon_kw),
            "reference": "oracle NumPy fp32, one fresh step on the same bf16 inputs"}
     if world > 1:
         unsharded = None
@@ -345,11 +368,16 @@ def parity_check(rf, dev, dist, rank: int, world: int) -> dict:
                 rf.distributed.use(prev)
         dist.barrier()
         if rank == 0:
-            out["sharded_vs_unsharded"] = max(rel_err(got[k], unsharded[k]) for k in PARITY_SHAPES)
+            held = [k for k in shapes if got[k] is not None]
+            out["sharded_vs_unsharded"] = max(rel_err(got[k], unsharded[k]) for k in held) if held else 0.0
+            out["sharded_leaves_compared"] = held
+            got = unsharded
     if rank == 0:
-        tx_o = O.OracleMuon(learning_rate=0.02, weight_decay=0.01, beta=0.95)
-        ref, _ = tx_o.update(g_np, tx_o.init(p_np), p_np, param_dtypes={k: "bfloat16" for k in PARITY_SHAPES})
-        errs = {k: rel_err(got[k], ref[k]) for k in PARITY_SHAPES}
+        okw = {"momentum_accumulator": muon_kw.get("momentum_accumulator", "ema"),
+               "nesterov": muon_kw.get("nesterov", True)}
+        tx_o = O.OracleMuon(learning_rate=0.02, weight_decay=0.01, beta=0.95, **okw)
+        ref, _ = tx_o.update(g_np, tx_o.init(p_np), p_np, param_dtypes={k: "bfloat16" for k in shapes})
+        errs = {k: rel_err(got[k], ref[k]) for k in shapes}
         out["rel_err"] = {k: float(f"{v:.3e}") for k, v in errs.items()}
         out["max_rel_err_muon"] = max(v for k, v in errs.items() if k != "norm")
         out["max_rel_err_adamw"] = errs["norm"]
@@ -372,13 +400,18 @@ def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
     """Same step through host buffers: pinned gradients copied H2D and the
     update tree copied D2H inside the timed region, every step."""
     torch.cuda.empty_cache()
-    host_g = map_shapes(shapes, lambda s: torch.empty(s, dtype=torch.bfloat16, pin_memory=True))
-    for hg, dg in zip(leaves_of(host_g), leaves_of(grad_sets[0])):
-        hg.copy_(dg)
     dev_g = grad_sets[1]
-    host_u = map_shapes(shapes, lambda s: torch.empty(s, dtype=torch.float32, pin_memory=True))
-    h2d = sum(t.numel() * t.element_size() for t in leaves_of(host_g))
-    d2h = sum(t.numel() * t.element_size() for t in leaves_of(host_u))
+    # Leaves this rank holds (under updates="owned" the others are meta).
+    real = [not t.is_meta for t in leaves_of(dev_g)]
+    host_g = [torch.empty(t.shape, dtype=torch.bfloat16, pin_memory=True) if r else None
+              for t, r in zip(leaves_of(grad_sets[0]), real)]
+    for hg, dg in zip(host_g, leaves_of(grad_sets[0])):
+        if hg is not None:
+            hg.copy_(dg)
+    host_u = [torch.empty(t.shape, dtype=torch.float32, pin_memory=True) if r else None
+              for t, r in zip(leaves_of(dev_g), real)]
+    h2d = sum(t.numel() * t.element_size() for t in host_g if t is not None)
+    d2h = sum(t.numel() * t.element_size() for t in host_u if t is not None)
     k = args.e2e_steps or max(2, min(args.steps, 5))
     upd, state = tx.update(dev_g, state, params)  # warm the output allocations
     del upd
@@ -386,11 +419,13 @@ def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(k):
-        for hg, dg in zip(leaves_of(host_g), leaves_of(dev_g)):
-            dg.copy_(hg, non_blocking=True)
+        for hg, dg in zip(host_g, leaves_of(dev_g)):
+            if hg is not None:
+                dg.copy_(hg, non_blocking=True)
         upd, state = tx.update(dev_g, state, params)
-        for hu, du in zip(leaves_of(host_u), leaves_of(upd)):
-            hu.copy_(du, non_blocking=True)
+        for hu, du in zip(host_u, leaves_of(upd)):
+            if hu is not None:
+                hu.copy_(du, non_blocking=True)
         upd = None  # the copies are stream-ordered before any reuse of these blocks
     e1.record()
     barrier()
@@ -413,8 +448,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--layers", type=int, default=32,
-                    help="reduced-size case for kernel profiles only (the headline is 32 layers)")
+    ap.add_argument("--workload", default="llama3_8b_muon_step", choices=sorted(WORKLOADS))
+    ap.add_argument("--layers", type=int, default=None,
+                    help="reduced-size case for kernel profiles only (the headline is the full model)")
     ap.add_argument("--vocab", type=int, default=128256)
     ap.add_argument("--preconditioning", default="frobenius", choices=["frobenius", "aol", "schatten", "spectral"])
     ap.add_argument("--adaptive", action="store_true")
@@ -442,21 +478,45 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        rf.distributed.configure()
+    shape_fn, muon_kw, baseline_cfg = WORKLOADS[args.workload]
+    owned_mode = args.workload == "llama3_70b_muon_step"
+    if owned_mode and world == 1 and args.layers is None:
+        raise SystemExit("llama3_70b_muon_step needs 8 GPUs (replicated updates do not fit one B200); "
+                         "use --layers for a reduced case")
+    if world > 1:
+        # The 70B tree runs with owners keeping their updates (no exchange):
+        # its float32 update tree (274 GB) does not fit one GPU.
+        rf.distributed.configure(updates="owned" if owned_mode else "all")
     rf.set_ns_precision(args.precision)
 
-    shapes = llama3_8b_shapes(args.layers, args.vocab)
+    full_size = args.layers is None and args.vocab == 128256
+    if args.workload == "llama3_8b_muon_step":
+        shapes = llama3_8b_shapes(32 if args.layers is None else args.layers, args.vocab)
+    else:
+        shapes = llama3_70b_shapes(80 if args.layers is None else args.layers)
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234)
+    gen.manual_seed(1234)  # data-parallel: every rank holds the same (reduced) gradients
 
-    def randn(s, scale=1.0):
-        t = torch.empty(s, dtype=torch.bfloat16, device=dev)
-        t.normal_(0.0, scale, generator=gen)
-        return t
-
-    params = map_shapes(shapes, lambda s: randn(s, 0.02))
-    grad_sets = [map_shapes(shapes, lambda s: randn(s)) for _ in range(2)]
     specs = muon_specs(shapes, rf)
+    if owned_mode and world > 1:
+        meta = map_shapes(shapes, lambda s: torch.empty(s, dtype=torch.bfloat16, device="meta"))
+        owners = rf.distributed.ownership(meta, specs, world)
+    else:
+        owners = map_shapes(shapes, lambda s: rank)
+
+    def leaf_maker(scale):
+        own = iter(leaves_of(owners))
+
+        def make(s):
+            if next(own) != rank:
+                return torch.empty(s, dtype=torch.bfloat16, device="meta")  # another rank's leaf
+            t = torch.empty(s, dtype=torch.bfloat16, device=dev)
+            t.normal_(0.0, scale, generator=gen)
+            return t
+        return make
+
+    params = map_shapes(shapes, leaf_maker(0.02))
+    grad_sets = [map_shapes(shapes, leaf_maker(1.0)) for _ in range(2)]
     variant = {}
     if args.preconditioning != "frobenius":
         variant["preconditioning"] = args.preconditioning
@@ -464,7 +524,8 @@ def main():
         variant["adaptive"] = True
     if args.mu_dtype != "float32":
         variant["mu_dtype"] = torch.bfloat16
-    tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95, muon_weight_dimension_numbers=specs, **variant)
+    tx = rf.muon(learning_rate=0.02, weight_decay=0.01, beta=0.95, muon_weight_dimension_numbers=specs, **muon_kw,
+                 **variant)
     state = tx.init(params)
     torch.cuda.synchronize()
 
@@ -521,11 +582,22 @@ def main():
     # ---- parity of the same code path, after (outside) the timed region ---
     del tx, state, params
     torch.cuda.empty_cache()
-    parity = None if args.no_parity else parity_check(rf, dev, dist, rank, world)
+    parity = None if args.no_parity else parity_check(
+        rf, dev, dist, rank, world, PARITY_SHAPES_70B if owned_mode else PARITY_SHAPES, muon_kw)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not owned_mode:
         cpu = cpu_layer_baseline()
+    n_layers = len(shapes["layers"])
+    workload = args.workload if full_size else f"{args.workload}_reduced_{n_layers}_layers_vocab_{args.vocab}"
+    model = ("Llama-3-8B" if args.workload == "llama3_8b_muon_step" else "Llama-3-70B") + \
+        f" ({n_layers} layers) parameter set"
+    transport = {"ce+owner_tail": ", copy-engine push of owners' float32 updates into IPC-mapped peer arenas "
+                                  "(AdamW split by element range)",
+                 "ce": ", copy-engine all-gather of 16-bit O into IPC-mapped peer buffers",
+                 "nccl": ", NCCL all-gather"}.get(rf.distributed.active_transport(), "") if world > 1 else ""
+    if owned_mode and world > 1:
+        transport = ", owners keep their leaves' updates (no exchange: the float32 update tree does not fit a GPU)"
 
     if rank == 0:
         out = {
@@ -541,17 +613,15 @@ def main():
             "vs_baseline": None,
             "dtype": f"{args.precision} NS operands, fp32 accumulate/state, bf16 params+grads",
             "data": "synthetic: N(0,1) bf16 grads (2 seeded sets), N(0,0.02) bf16 params",
-            "config": {"workload": ("llama3_8b_muon_step" if (args.layers, args.vocab) == (32, 128256)
-                                    else f"reduced_{args.layers}_layers_vocab_{args.vocab}")
+            "config": {"workload": workload
                        + "".join(f"+{k}={v if k != 'mu_dtype' else args.mu_dtype}" for k, v in variant.items()),
-                       "model": f"Llama-3-8B ({args.layers} layers) parameter set",
-                       "muon_leaves": 7 * args.layers, "adam_leaves": 2 * args.layers + 3, "ns_steps": 5,
-                       "ns_coeffs": "standard",
-                       "l2": "inputs (16 GB grads) >> 126 MB L2; no flush",
-                       "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)"
-                       + ({"ce": ", copy-engine all-gather into IPC-mapped peer buffers",
-                           "nccl": ", NCCL all-gather"}.get(rf.distributed.active_transport(), "")
-                          if world > 1 else "")},
+                       "baseline_config": baseline_cfg,
+                       "model": model,
+                       "muon_leaves": len(muon_matrix_shapes(shapes)),
+                       "adam_leaves": len(leaves_of(shapes)) - len(muon_matrix_shapes(shapes)), "ns_steps": 5,
+                       "ns_coeffs": "standard", "options": {k: v for k, v in muon_kw.items()},
+                       "l2": "inputs (>= 16 GB grads) >> 126 MB L2; no flush",
+                       "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)" + transport},
             "ns_tflops_algorithmic": round(ns_alg_flops(shapes) / (ms * 1e-3) / 1e12, 1),
             "roofline": {
                 "bound": "tensor",
@@ -566,7 +636,7 @@ def main():
                 "gemm_ms_per_step": round(prof["gemm_ms"] / args.steps, 2),
                 # DRAM read+write bytes per launch of the 4096x14336 sub-batch
                 # stages (80% of the step's FLOPs): see TRAFFIC_PER_LAUNCH.
-                "traffic": TRAFFIC_PER_LAUNCH if (args.layers, args.vocab) == (32, 128256) else None,
+                "traffic": TRAFFIC_PER_LAUNCH if (full_size and not owned_mode) else None,
                 "traffic_unit": "bytes per launch",
             },
             "gpu_launches": launches,

@@ -122,6 +122,9 @@ struct Plan {
 
 static size_t ns_elem(int precision) { return precision == RF_NS_F32 ? 4 : 2; }
 
+// Workspace budget of one shape sub-batch (see build_plan).
+constexpr size_t kMaxSubBatchBytes = size_t(16) << 30;
+
 static int64_t chunks_per_mat(int64_t numel) { return ceil_div(numel, kChunk); }
 
 static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan& P, int regions = 1) {
@@ -156,7 +159,16 @@ static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan
   for (size_t gi = 0; gi < P.groups.size(); ++gi) {
     GroupPlan& gp = P.groups[gi];
     const auto& mem = members[gi];
-    const int nsub = int(ceil_div(int64_t(mem.size()), kMaxLeavesPerLaunch));
+    // Sub-batches: at most kMaxLeavesPerLaunch leaves, and a workspace region
+    // (X0, X1, A~, B~ of every matrix) of about kMaxSubBatchBytes, so that
+    // wide groups (e.g. thirty 8192x28672 matrices) leave room in HBM for
+    // the state and the updates.
+    int64_t mats = 0;
+    for (int li : mem) mats += P.leaves[li].batch;
+    const double per_mat = double(2 * gp.mp * gp.np + 2 * gp.mp * gp.mp) * double(es);
+    const int64_t by_bytes = int64_t(std::ceil(double(mats) * per_mat / double(kMaxSubBatchBytes)));
+    const int nsub = int(std::min<int64_t>(int64_t(mem.size()),
+                                           std::max(ceil_div(int64_t(mem.size()), kMaxLeavesPerLaunch), by_bytes)));
     const size_t per = (mem.size() + nsub - 1) / nsub;  // even split
     for (size_t s = 0; s < mem.size(); s += per)
       gp.subs.emplace_back(mem.begin() + s, mem.begin() + std::min(mem.size(), s + per));

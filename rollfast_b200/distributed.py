@@ -51,6 +51,7 @@ class ShardContext:
     errors: "ErrorWatch" = None
     steps: int = 0                    # sharded updates run with this context
     owner_tail: bool = True           # copy-engine transport: owners push final float32 updates
+    updates: str = "all"              # "all": every rank returns the whole tree; "owned": owners only
 
     def close(self) -> None:
         """Releases the plans' peer mappings (collective when any exist)."""
@@ -114,7 +115,7 @@ TRANSPORTS = ("auto", "ce", "nccl")
 
 
 def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None = None,
-              transport: str | None = None, owner_tail: bool | None = None) -> ShardContext:
+              transport: str | None = None, owner_tail: bool | None = None, updates: str = "all") -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
 
     ``transport``: how owners' leaves reach the other ranks: ``"ce"`` (copy
@@ -132,6 +133,13 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
     owners exchange 16-bit O and every rank runs the tail over all leaves
     into fresh buffers.
 
+    ``updates="owned"``: no exchange at all; each rank updates and returns
+    only the leaves it owns (``ownership``), for models whose replicated
+    update tree does not fit one GPU (Llama-3-70B: 274 GB of float32
+    updates).  Leaves a rank does not own may be passed as meta tensors
+    (shape only) in the gradients, parameters and state, and come back as
+    meta tensors in the updates; their momentum is not advanced there.
+
     ``reserve_sms``: SMs the Newton-Schulz GEMM grid leaves free so the
     all-gather (NCCL) runs beside it without displacing GEMM CTAs; default:
     the NCCL channel cap ``NCCL_MAX_NCHANNELS`` when that is set, else 0.
@@ -147,6 +155,8 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
     transport = transport.lower()
     if transport not in TRANSPORTS:
         raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
+    if updates not in ("all", "owned"):
+        raise ValueError(f"updates must be 'all' or 'owned', got {updates!r}")
     import torch.distributed as dist
 
     global _ctx
@@ -156,7 +166,7 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
         _ctx.close()
     _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
                         buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)), transport=transport,
-                        owner_tail=bool(owner_tail))
+                        owner_tail=bool(owner_tail), updates=updates)
     return _ctx
 
 
@@ -577,6 +587,92 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
     ctx.owned_state = owned
     ctx.errors.snapshot(compute, ctx.steps)
     return _finish_leaves(ml), a_outs
+
+
+def owner_ranks(muon_shapes, adam_numels, world_size: int) -> tuple[list[int], list[int]]:
+    """Owners under ``updates="owned"``: Muon leaves (``(batch, rows, cols)``
+    in tree order) by longest-processing-time-first on their Newton-Schulz
+    FLOPs, the same assignment every sharded mode uses; AdamW leaves by
+    longest-processing-time-first on their element counts."""
+    muon = lpt_assign([ns_flops(*s) for s in muon_shapes], world_size) if muon_shapes else []
+    adam = lpt_assign(list(adam_numels), world_size) if adam_numels else []
+    return muon, adam
+
+
+def ownership(params, muon_weight_dimension_numbers=None, world_size: int | None = None):
+    """A tree like ``params`` holding the rank that owns each leaf under
+    ``configure(updates="owned")`` for a ``muon(...)`` built with the same
+    ``muon_weight_dimension_numbers`` (None for aux leaves).  Shapes and
+    dtypes are all it reads, so meta tensors work: a caller can allocate
+    gradients, parameters and state only for the leaves it owns."""
+    from .dimension_numbers import _compute_matrix_layout, _make_matrix_partition_fns
+    from .muon import _flatten_specs
+    from .tree import is_aux_leaf, tree_flatten, tree_unflatten
+
+    if world_size is None:
+        world_size = _ctx.world_size if _ctx is not None else 1
+    part = _make_matrix_partition_fns(muon_weight_dimension_numbers, "muon")
+    leaves, treedef = tree_flatten(params, is_leaf=is_aux_leaf)
+    labels = tree_flatten(part.labels(params), is_leaf=lambda x: x is None or isinstance(x, str))[0]
+    specs = _flatten_specs(part.masked_specs(params), len(leaves))
+    muon_pos, muon_shapes, adam_pos, adam_numels = [], [], [], []
+    for i, (x, lab, spec) in enumerate(zip(leaves, labels, specs)):
+        if is_aux_leaf(x):
+            continue
+        if lab == "muon":
+            muon_pos.append(i)
+            muon_shapes.append(_compute_matrix_layout(x.shape, x.dtype, spec).flat_shape)
+        else:
+            adam_pos.append(i)
+            adam_numels.append(x.numel())
+    mo, ao = owner_ranks(muon_shapes, adam_numels, world_size)
+    out = [None] * len(leaves)
+    for i, r in zip(muon_pos, mo):
+        out[i] = r
+    for i, r in zip(adam_pos, ao):
+        out[i] = r
+    return tree_unflatten(treedef, out)
+
+
+def owned_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds=None):
+    """``updates="owned"``: momentum + Newton-Schulz + fused tail for the Muon
+    leaves this rank owns and AdamW for the AdamW leaves it owns, into fresh
+    float32 buffers; every other leaf's update is a meta tensor.  No data
+    crosses ranks."""
+    from .adam import run_adam
+    from .base import require_cuda
+    from .muon import _finish_leaves, _leaf_table, run_muon_table
+
+    mo, ao = owner_ranks([L.layout.flat_shape for L in ml], [it[0].numel() for it in a_items], ctx.world_size)
+    mine = [i for i, r in enumerate(mo) if r == ctx.rank]
+    for i in mine:
+        require_cuda(ml[i].g, "gradient of an owned leaf")
+    ml = [L._replace(out=torch.empty(L.out.shape, dtype=torch.float32, device=L.g.device)) if r == ctx.rank else L
+          for L, r in zip(ml, mo)]
+    if mine:
+        sub = [ml[i] for i in mine]
+        arr = _leaf_table(sub, [scales[i] for i in mine], [decays[i] for i in mine], [decay_f32[i] for i in mine])
+        run_muon_table(arr, len(sub), prm, sub[0].g.device)
+    outs = []
+    for L, r in zip(ml, mo):
+        if r == ctx.rank:
+            outs.append(_finish_leaves([L])[0])
+        else:
+            outs.append(torch.empty(L.shape, dtype=torch.float32, device="meta"))
+    a_outs, items, seeds = [], [], []
+    for j, (it, r) in enumerate(zip(a_items, ao)):
+        if r == ctx.rank:
+            require_cuda(it[0], "gradient of an owned leaf")
+            o = torch.empty(it[0].shape, dtype=torch.float32, device=it[0].device)
+            items.append((*it[:4], o, *it[5:]))
+            if a_seeds is not None:
+                seeds += [a_seeds[2 * j], a_seeds[2 * j + 1]]
+        else:
+            o = torch.empty(it[0].shape, dtype=torch.float32, device="meta")
+        a_outs.append(o)
+    run_adam(items, seeds=seeds if a_seeds is not None else None, **adam_kw)
+    ctx.owned_state = []
+    return outs, a_outs
 
 
 def consolidate_momentum(ctx: ShardContext | None = None) -> int:

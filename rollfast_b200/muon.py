@@ -149,13 +149,17 @@ def _as_matrix(t: torch.Tensor, lay) -> torch.Tensor:
     return t.permute(lay.perm).contiguous().view(lay.flat_shape)
 
 
-def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str):
+def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str, allow_meta: bool = False):
+    """Muon leaves in their (batch, R, O) layout.  ``allow_meta``: leaves held
+    as meta tensors (shape only, no data: not owned by this rank under
+    ``distributed.configure(updates="owned")``) are kept as meta."""
     out = []
     for i, (g, spec) in enumerate(zip(leaves, specs)):
         if is_aux_leaf(g):
             continue
         _validate_matrix_operand(g, spec, transform_name)
-        require_cuda(g, "gradient")
+        if not (allow_meta and isinstance(g, torch.Tensor) and g.is_meta):
+            require_cuda(g, "gradient")
         lay = _compute_matrix_layout(g.shape, g.dtype, spec)
         mu_state = mus[i]
         p = ps[i] if ps is not None else None
@@ -167,7 +171,7 @@ def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str):
             mu=mu_state.view(lay.flat_shape) if lay.is_identity else _as_matrix(mu_state, lay),
             mu_state=mu_state,
             p=None if p is None else _as_matrix(p, lay),
-            out=torch.empty(lay.flat_shape, dtype=torch.float32, device=g.device),
+            out=torch.empty(lay.flat_shape, dtype=torch.float32, device="meta" if allow_meta else g.device),
             layout=lay,
             shape=tuple(g.shape),
             spec=spec,
@@ -463,7 +467,10 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         for g, s in zip(muon_leaves, muon_specs):
             if g is not None:
                 _validate_matrix_operand(g, s, "scale_by_muon")
-        ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon")
+        ctx = distributed.current()
+        sharded = ctx is not None and ctx.world_size > 1
+        owned_only = sharded and ctx.updates == "owned"
+        ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon", allow_meta=owned_only)
         ml, muon_key_next = _seed_leaves(ml, muon_st.key)
         scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
         # add_decayed_weights of each branch: a constant, or a schedule at the
@@ -483,7 +490,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         for i, (g, l) in enumerate(zip(leaves, lab)):
             if is_aux_leaf(g) or l != "adam":
                 continue
-            require_cuda(g, "gradient")
+            if not (owned_only and g.is_meta):
+                require_cuda(g, "gradient")
             if g.dtype.is_complex:
                 raise NotImplementedError("complex leaves are not on the B200 hot path")
             p = ps[i]
@@ -499,15 +507,15 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         adam_kw = dict(b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
                        count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
 
-        ctx = distributed.current()
-        sharded = ctx is not None and ctx.world_size > 1
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
                                  ns_steps=ns_steps, lr=lr, fuse_tail=1,
                                  reserve_sms=ctx.reserve_sms if sharded else 0,
                                  preconditioning=preconditioning, adaptive=adaptive)
         res = None
-        if sharded and ctx.owner_tail and ctx.transport in ("ce", "auto") and not adaptive and (ml or a_items):
+        if owned_only:
+            res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds)
+        elif sharded and ctx.owner_tail and ctx.transport in ("ce", "auto") and not adaptive and (ml or a_items):
             res = distributed.sharded_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32, a_items, adam_kw,
                                              a_seeds)
             if res is None:

@@ -208,3 +208,45 @@ def test_gloo_world2_consolidate_momentum_from_owners():
     for p in procs:
         p.join(timeout=60)
     assert results == {0: True, 1: True}
+
+
+def llama70b_meta_tree(layers=80):
+    d, kv, ff = 8192, 1024, 28672
+    mk = lambda *s: torch.empty(s, dtype=torch.bfloat16, device="meta")  # noqa: E731
+    tree = {"final_norm": mk(d)}
+    for i in range(layers):
+        tree[f"l{i:02d}"] = {"q": mk(d, d), "k": mk(d, kv), "v": mk(d, kv), "o": mk(d, d), "gate": mk(d, ff),
+                             "up": mk(d, ff), "down": mk(ff, d), "attn_norm": mk(d), "mlp_norm": mk(d)}
+    return tree
+
+
+def test_ownership_of_llama70b_is_flop_balanced_and_matches_the_update_planner():
+    """updates="owned": the public ownership tree, from
+    shapes alone (meta tensors), equals the assignment the sharded update
+    makes, and balances the 80-layer tree exactly over 8 ranks
+    (30 / 20 / 20 gate-up-down / q-o / k-v matrices per rank)."""
+    import rollfast_b200 as rf
+    from rollfast_b200.distributed import owner_ranks, ownership
+    from rollfast_b200.tree import tree_leaves
+
+    tree = llama70b_meta_tree()
+    own = ownership(tree, world_size=8)
+    owners = tree_leaves(own)
+    flat = tree_leaves(tree)
+    muon_shapes = [tuple([1, *x.shape]) for x in flat if x.ndim == 2]
+    adam = [x.numel() for x in flat if x.ndim == 1]
+    mo, ao = owner_ranks(muon_shapes, adam, 8)
+    assert [r for r, x in zip(owners, flat) if x.ndim == 2] == mo
+    assert [r for r, x in zip(owners, flat) if x.ndim == 1] == ao
+    loads = [0] * 8
+    for s, r in zip(muon_shapes, mo):
+        loads[r] += ns_flops(*s)
+    assert max(loads) == min(loads)
+    counts = {}
+    for s, r in zip(muon_shapes, mo):
+        counts.setdefault(r, []).append(min(s[1:]) * max(s[1:]))
+    assert all(len(v) == 70 for v in counts.values())
+    # A meta tree initialises without allocating: the state of leaves a rank
+    # does not own can stay meta.
+    st = rf.muon(learning_rate=0.01).init({"w": torch.empty(64, 128, device="meta")})
+    assert st.inner_states["muon"].inner_state[0][0].mu["w"].is_meta

@@ -112,3 +112,82 @@ def test_sharded_update_matches_single_gpu_on_two_gpus(transport, owner_tail):
     for p in procs:
         p.join(timeout=120)
     assert results == {0: True, 1: True}, results
+
+
+def _owned_worker(rank, world, port, q):
+    """updates="owned" on a 2-layer Llama-3-70B-shaped tree (BASELINE config
+    5 options: heavy-ball momentum, Nesterov off): each rank's owned leaves
+    equal the unsharded run's bit for bit, both when the rank holds the whole
+    tree and when the leaves it does not own are meta tensors."""
+    import datetime
+
+    import torch.distributed as dist
+
+    import rollfast_b200 as rf
+    from rollfast_b200.tree import tree_flatten, tree_unflatten
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["ROLLFAST_NS_KERNEL"] = "2"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        d, kv, ff = 8192, 1024, 28672
+        shapes = {f"l{i}": {"q": (d, d), "k": (d, kv), "v": (d, kv), "o": (d, d), "gate": (d, ff), "up": (d, ff),
+                            "down": (ff, d), "norm": (d,)} for i in range(2)}
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        mk = lambda s, sc: (torch.randn(s, device=dev, generator=g) * sc).to(torch.bfloat16)  # noqa: E731
+        params = {l: {k: mk(s, 0.02) for k, s in t.items()} for l, t in shapes.items()}
+        grads = {l: {k: mk(s, 1.0) for k, s in t.items()} for l, t in shapes.items()}
+        kw = dict(learning_rate=0.02, weight_decay=0.01, momentum_accumulator="heavy_ball", nesterov=False)
+        ref_tx = rf.muon(**kw)
+        u_ref, _ = ref_tx.update(grads, ref_tx.init(params), params)
+        torch.cuda.synchronize()
+        owners = tree_flatten(rf.distributed.ownership(params, world_size=world))[0]
+        ctx = rf.distributed.configure(updates="owned")
+        ok = sorted(set(owners)) == list(range(world))
+        # (a) the whole tree held on every rank
+        tx = rf.muon(**kw)
+        u, _ = tx.update(grads, tx.init(params), params)
+        torch.cuda.synchronize()
+        for r, a, b in zip(owners, tree_flatten(u)[0], tree_flatten(u_ref)[0]):
+            ok &= (not a.is_meta and bool(torch.equal(a, b))) if r == rank else a.is_meta
+        # (b) leaves of other ranks as meta tensors (no memory for them here)
+        def own_only(tree):
+            flat, tdef = tree_flatten(tree)
+            return tree_unflatten(tdef, [x if r == rank else torch.empty(x.shape, dtype=x.dtype, device="meta")
+                                         for x, r in zip(flat, owners)])
+        p2, g2 = own_only(params), own_only(grads)
+        tx2 = rf.muon(**kw)
+        u2, _ = tx2.update(g2, tx2.init(p2), p2)
+        torch.cuda.synchronize()
+        for r, a, b in zip(owners, tree_flatten(u2)[0], tree_flatten(u_ref)[0]):
+            ok &= (not a.is_meta and bool(torch.equal(a, b))) if r == rank else a.is_meta
+        del ctx
+        rf.distributed.clear()
+        q.put((rank, bool(ok)))
+    except Exception as exc:  # report instead of hanging the other rank
+        q.put((rank, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_owned_updates_match_single_gpu_on_llama70b_layers():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_owned_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: True, 1: True}, results
