@@ -89,13 +89,26 @@ def llama3_70b_shapes(layers: int = 80):
     return {"layers": [dict(layer) for _ in range(layers)], "final_norm": (8192,)}
 
 
+def gpt2_small_shapes(layers: int = 12, vocab: int = 50257):
+    """12 scanned layers (stacked leaves, reduction axis
+    1, output axis 2) of 768x2304 qkv, 768x768 proj, 768x3072 fc and 3072x768
+    fc_out; LayerNorm gains and biases (stacked vectors) and the 50257x768
+    embedding to AdamW."""
+    L = layers
+    return {"layers": [{"qkv": (L, 768, 2304), "proj": (L, 768, 768), "fc": (L, 768, 3072),
+                        "fc_out": (L, 3072, 768), "ln1_g": (L, 768), "ln1_b": (L, 768), "ln2_g": (L, 768),
+                        "ln2_b": (L, 768)}], "final_norm": (768,), "embed": (vocab, 768)}
+
+
 def muon_specs(shapes, rf, name=None):
     """2-D weight matrices -> Muon; vectors, embed and unembed -> AdamW."""
     if isinstance(shapes, dict):
         return {k: muon_specs(v, rf, k) for k, v in shapes.items()}
     if isinstance(shapes, list):
         return [muon_specs(v, rf, name) for v in shapes]
-    if len(shapes) == 2 and name not in ("embed", "unembed"):
+    if len(shapes) == 3:  # a stack of scanned layers: (layer, rows, cols)
+        return rf.MatrixDimensionNumbers(1, 2)
+    if len(shapes) == 2 and name not in ("embed", "unembed") and not name.startswith("ln"):
         return rf.MatrixDimensionNumbers()
     return None
 
@@ -124,14 +137,15 @@ def leaves_of(tree):
 
 def ns_alg_flops(shapes, steps=5):
     tot = 0
-    for s in leaves_of(muon_matrix_shapes(shapes)):
-        m, n = min(s), max(s)
-        tot += (4 * m * m * n + 2 * m ** 3) * steps
+    for s in muon_matrix_shapes(shapes):
+        b = s[0] if len(s) == 3 else 1
+        m, n = min(s[-2:]), max(s[-2:])
+        tot += b * (4 * m * m * n + 2 * m ** 3) * steps
     return tot
 
 
 def muon_matrix_shapes(shapes):
-    return [s for layer in shapes["layers"] for k, s in layer.items() if len(s) == 2]
+    return [s for layer in shapes["layers"] for k, s in layer.items() if len(s) >= 2 and not k.startswith("ln")]
 
 
 WORKLOADS = {
@@ -139,6 +153,7 @@ WORKLOADS = {
     "llama3_8b_muon_step": (llama3_8b_shapes, {}, "configs[2]"),
     "llama3_70b_muon_step": (llama3_70b_shapes, {"momentum_accumulator": "heavy_ball", "nesterov": False},
                              "configs[4]"),
+    "gpt2_small_muon_step": (gpt2_small_shapes, {"ns_coeffs": "polar_express"}, "configs[1]"),
 }
 
 
@@ -489,9 +504,11 @@ def main():
         rf.distributed.configure(updates="owned" if owned_mode else "all")
     rf.set_ns_precision(args.precision)
 
-    full_size = args.layers is None and args.vocab == 128256
+    full_size = args.layers is None and (args.vocab == 128256 or args.workload != "llama3_8b_muon_step")
     if args.workload == "llama3_8b_muon_step":
         shapes = llama3_8b_shapes(32 if args.layers is None else args.layers, args.vocab)
+    elif args.workload == "gpt2_small_muon_step":
+        shapes = gpt2_small_shapes(12 if args.layers is None else args.layers)
     else:
         shapes = llama3_70b_shapes(80 if args.layers is None else args.layers)
     gen = torch.Generator(device=dev)
@@ -583,15 +600,16 @@ def main():
     del tx, state, params
     torch.cuda.empty_cache()
     parity = None if args.no_parity else parity_check(
-        rf, dev, dist, rank, world, PARITY_SHAPES_70B if owned_mode else PARITY_SHAPES, muon_kw)
+        rf, dev, dist, rank, world, PARITY_SHAPES_70B if owned_mode else PARITY_SHAPES,
+        {k: v for k, v in muon_kw.items() if k != "ns_coeffs"})
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not owned_mode:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "llama3_8b_muon_step":
         cpu = cpu_layer_baseline()
-    n_layers = len(shapes["layers"])
+    n_layers = len(shapes["layers"]) if args.workload != "gpt2_small_muon_step" else shapes["layers"][0]["qkv"][0]
     workload = args.workload if full_size else f"{args.workload}_reduced_{n_layers}_layers_vocab_{args.vocab}"
-    model = ("Llama-3-8B" if args.workload == "llama3_8b_muon_step" else "Llama-3-70B") + \
-        f" ({n_layers} layers) parameter set"
+    model = {"llama3_8b_muon_step": "Llama-3-8B", "llama3_70b_muon_step": "Llama-3-70B",
+             "gpt2_small_muon_step": "GPT-2 small"}[args.workload] + f" ({n_layers} layers) parameter set"
     transport = {"ce+owner_tail": ", copy-engine push of owners' float32 updates into IPC-mapped peer arenas "
                                   "(AdamW split by element range)",
                  "ce": ", copy-engine all-gather of 16-bit O into IPC-mapped peer buffers",
@@ -619,7 +637,8 @@ def main():
                        "model": model,
                        "muon_leaves": len(muon_matrix_shapes(shapes)),
                        "adam_leaves": len(leaves_of(shapes)) - len(muon_matrix_shapes(shapes)), "ns_steps": 5,
-                       "ns_coeffs": "standard", "options": {k: v for k, v in muon_kw.items()},
+                       "ns_coeffs": muon_kw.get("ns_coeffs", "standard"),
+                       "options": {k: v for k, v in muon_kw.items() if k != "ns_coeffs"},
                        "l2": "inputs (>= 16 GB grads) >> 126 MB L2; no flush",
                        "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)" + transport},
             "ns_tflops_algorithmic": round(ns_alg_flops(shapes) / (ms * 1e-3) / 1e12, 1),

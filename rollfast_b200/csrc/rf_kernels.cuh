@@ -361,22 +361,40 @@ __device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const Fin
 
 // Final-stage epilogue for one 32-column chunk held by a warp: lane l owns
 // row row0 + l (columns col0..col0+31, values o[], already scaled to O).  A
-// plain leaf is stored as one 32-element run per lane.  A transposed leaf
-// holds NS element (r, c) at c * m + r: lanes own consecutive rows, so for
-// each column the warp's 32 stores (and the fused tail's parameter loads) are
-// one contiguous run of the leaf, without a transpose through shared memory.
+// transposed leaf is stored along its rows, i.e. along the NS columns, so the
+// warp's 32x32 block is transposed through `stg` (32 x 33 floats, per warp)
+// and every lane writes one 32-element run.
 __device__ __forceinline__ void final_chunk(const NsGemmArgs& a, const FinalLeaf& L, int64_t bi, int64_t row0,
-                                           int64_t col0, int lane, const float* o) {
+                                           int64_t col0, int lane, const float* o, float* stg) {
   const int64_t mat = bi * a.m * a.n;
-  const int64_t r = row0 + lane;
-  if (r >= a.m) return;
-  if (!L.transposed && L.vec_ok && col0 + 32 <= a.n) {
-    final_store_run32(a, L, mat + r * a.n + col0, o);
+  if (!L.transposed) {
+    const int64_t r = row0 + lane;
+    if (r >= a.m) return;
+    if (L.vec_ok && col0 + 32 <= a.n) {
+      final_store_run32(a, L, mat + r * a.n + col0, o);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (col0 + k < a.n) final_store(a, L, bi, r, col0 + k, o[k]);
+    }
     return;
   }
 #pragma unroll
-  for (int k = 0; k < 32; ++k)
-    if (col0 + k < a.n) final_store(a, L, bi, r, col0 + k, o[k]);
+  for (int k = 0; k < 32; ++k) stg[lane * 33 + k] = o[k];
+  __syncwarp();
+  float t[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) t[i] = stg[i * 33 + lane];
+  __syncwarp();
+  const int64_t c = col0 + lane;
+  if (c >= a.n) return;
+  if (L.vec_ok && row0 + 32 <= a.m) {
+    final_store_run32(a, L, mat + c * a.m + row0, t);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (row0 + i < a.m) final_store(a, L, bi, row0 + i, c, t[i]);
+  }
 }
 
 }  // namespace rf

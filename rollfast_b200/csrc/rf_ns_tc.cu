@@ -35,7 +35,8 @@ constexpr int B_BYTES = BN * BK * 2;             // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;   // 48 KB
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // per-warp 32x32 transpose buffers
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/ + EPI_STAGE_BYTES;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct TcParams {
@@ -226,7 +227,7 @@ __device__ __forceinline__ void record_error(int code, volatile int* abort_flag)
 // general (fused a X + B X), final (O, or the fused tail, into the leaf).
 template <typename T>
 __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, int64_t g, int64_t row0, int64_t col0,
-                                               int lane, int fl, const float* v) {
+                                               int lane, int fl, const float* v, float* stg) {
   const T* aux = static_cast<const T*>(a.aux);
   T* out = static_cast<T*>(a.out);
   const int64_t ldc = sym ? a.mp : a.np;
@@ -281,7 +282,7 @@ __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, in
   const FinalLeaf& L = a.final_leaf[fl];
 #pragma unroll
   for (int k = 0; k < 32; ++k) f[k] *= a.out_scale;
-  final_chunk(a, L, g - L.group_mat_begin, row0, col0, lane, f);
+  final_chunk(a, L, g - L.group_mat_begin, row0, col0, lane, f, stg);
 }
 
 template <typename T>
@@ -294,6 +295,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc full, [2S+2..2S+4) acc empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 4 x 32x33 floats
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -428,6 +430,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     int acc = 0;
     uint32_t acc_phase = 0;
+    float* stg = epi_stage + (warp - 2) * (32 * 33);
     for (int64_t t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
       int64_t g;
       int I, J;
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         float v[32];
         __syncwarp();  // tcgen05.ld is warp-collective; lanes may have diverged on the diagonal
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + ch * 32), v);
-        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * BN + ch * 32, lane, fl, v);
+        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * BN + ch * 32, lane, fl, v, stg);
       }
       tc_fence_before();
       mbar_arrive(acce0 + 8 * acc);
@@ -480,13 +483,13 @@ namespace tc2 {
 #endif
 constexpr int BM = 128;                  // rows per CTA (256 per pair)
 constexpr int BNH = 128;                 // B rows/cols per CTA (256 per pair)
-constexpr int BK = 64, STAGES = RF_TC2_STAGES;  // compile-time pipeline depth (6: 198 KB of shared memory)
+constexpr int BK = 64, STAGES = RF_TC2_STAGES;  // pipeline depth (5, 6 and 7 measured alike)
 constexpr int A_BYTES = BM * BK * 2;     // 16 KB
 constexpr int B_BYTES = BNH * BK * 2;    // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + tc::EPI_STAGE_BYTES;
 static_assert(SMEM_BYTES <= 232448, "dynamic shared memory per CTA is at most 227 KB");
 
 using tc::kTimeoutNs;
@@ -590,6 +593,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   // [0,S) full (leader), [S,2S) empty, [2S,2S+2) acc full, [2S+2,2S+4) acc empty (leader)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);  // 4 x 32x33 floats
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * STAGES), acce0 = smem_u32(bars + 2 * STAGES + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -731,6 +735,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    float* stg = epi_stage + (warp - 2) * (32 * 33);
     for (int64_t t = pair; t < P.total_tiles; t += npairs) {
       int64_t g;
       int I, J;
@@ -747,7 +752,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         float v[32];
         __syncwarp();
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * 256 + ch * 32), v);
-        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * 256 + ch * 32, lane, fl, v);
+        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * 256 + ch * 32, lane, fl, v, stg);
       }
       tc_fence_before();
       __syncwarp();
