@@ -80,6 +80,13 @@ typedef struct rf_muon_leaf {
    * with a Python-float weight decay, weakly typed); 1: formed in float32 (a
    * schedule whose value is a float32 array, strongly typed). */
   int32_t decay_in_f32;
+  /* Magma (src/rollfast/optim/magma.py:16-132), NULL when off: the leaf's
+   * score (one float32 in device memory, read and updated in place: score <-
+   * 0.9 score + 0.1 sigmoid(cos(g, mu_t) / magma_tau)), and its Bernoulli
+   * draw for this step (magma_keep 0 or 1); the leaf's update is scaled by
+   * magma_keep * score after the decay and before the learning rate. */
+  float* magma_score;
+  int32_t magma_keep;
 } rf_muon_leaf;
 
 /* Newton-Schulz preconditioning (orthogonalization.py:24, 153-176, 233-250). */
@@ -120,6 +127,7 @@ typedef struct rf_muon_params {
    * Nesterov / bias-corrected direction; the NS final epilogue then writes O
    * and a separate pass applies the factor and the tail. */
   int32_t adaptive;
+  float magma_tau;  /* Magma temperature (muon.py:178), used by leaves with a magma_score */
 } rf_muon_params;
 
 /* Bytes of workspace rf_muon_update needs for these leaves and precision
@@ -205,6 +213,10 @@ typedef struct rf_adam_leaf {
    * the array masks of the in-transform decay (utils.py:79-90, 173-197:
    * where(mask, u + wd * p, u)); NULL: every element. */
   const uint8_t* decay_mask;
+  /* Magma (adam.py:204-215), as in rf_muon_leaf; needs the workspace of
+   * rf_adam_params. */
+  float* magma_score;
+  int32_t magma_keep;
 } rf_adam_leaf;
 typedef struct rf_adam_params {
   /* b1, b2 as the caller's double-precision scalars: the reference forms
@@ -217,7 +229,13 @@ typedef struct rf_adam_params {
   int32_t nesterov;
   float lr;
   int32_t max_ctas_per_sm;  /* as for rf_muon_tail */
+  float magma_tau;
+  /* Device workspace for the Magma reductions (sized by
+   * rf_adamw_workspace_size; may be NULL / 0 when no leaf uses Magma). */
+  void* workspace;
+  size_t workspace_bytes;
 } rf_adam_params;
+rf_status rf_adamw_workspace_size(const rf_adam_leaf* leaves, int32_t n_leaves, size_t* bytes);
 rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
                           void* stream);
 

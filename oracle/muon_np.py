@@ -45,6 +45,7 @@ __all__ = [
     "shape_scale_factor",
     "adam_leaf_update",
     "pow32",
+    "magma_leaf",
     "decay_at",
     "decay_term",
     "in_transform_decay",
@@ -586,6 +587,29 @@ def in_transform_decay(u: np.ndarray, p: np.ndarray, wd_step: float, mask=True) 
     uf = np.asarray(u, np.float32)
     dec = (uf + (np.float32(wd_step) * np.asarray(p, np.float32)).astype(np.float32)).astype(np.float32)
     return np.where(np.asarray(mask, dtype=bool), dec, uf).astype(np.float32)
+
+
+def magma_leaf(g, mu_new, delta, score_prev, keep, tau: float = 2.0):
+    """magma.py:86-128 for one leaf, its Bernoulli draw ``keep`` given (the
+    reference draws it from JAX's Threefry stream): the cosine between the
+    raw gradient and the new first moment, the score EMA
+    ``0.9 s + 0.1 sigmoid(cos / tau)``, and ``(keep * s_new) * delta``.
+    The three inner products are summed in float64 and rounded to float32
+    (JAX's float32 reduction order is not pinned).  Returns
+    ``(masked delta, new score)``."""
+    gf = np.asarray(g, np.float64).ravel()
+    mf = np.asarray(mu_new, np.float32).astype(np.float64).ravel()
+    dot = np.float32(np.dot(gf, mf))
+    ng = np.float32(np.dot(gf, gf))
+    nm = np.float32(np.dot(mf, mf))
+    denom = np.maximum(np.float32(np.sqrt(ng)) * np.float32(np.sqrt(nm)), np.float32(1e-12))
+    with np.errstate(invalid="ignore", divide="ignore"):
+        cos = np.float32(dot / denom)
+    cos = np.float32(np.clip(np.nan_to_num(cos, nan=0.0), -1.0, 1.0))
+    s_tilde = np.float32(1.0 / (1.0 + np.exp(-np.float64(cos / np.float32(tau)))))
+    s_new = np.float32(np.float32(0.9) * np.float32(score_prev) + np.float32(0.1) * s_tilde)
+    fac = np.float32(np.float32(1.0 if keep else 0.0) * s_new)
+    return (fac * np.asarray(delta, np.float32)).astype(np.float32), s_new
 
 
 def adam_leaf_update(g, mu, nu, count: int, *, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0,

@@ -37,6 +37,7 @@ EXPORTED = (
     "rf_newton_schulz_noalloc",
     "rf_muon_tail",
     "rf_adamw_update",
+    "rf_adamw_workspace_size",
     "rf_last_error",
     "rf_version",
     "rf_kernel_launch_count",
@@ -88,6 +89,8 @@ class RfMuonLeaf(ctypes.Structure):
         ("mu_dtype", ctypes.c_int32),
         ("sr_seed", ctypes.c_uint64),
         ("decay_in_f32", ctypes.c_int32),
+        ("magma_score", ctypes.c_void_p),
+        ("magma_keep", ctypes.c_int32),
     ]
 
 
@@ -108,6 +111,7 @@ class RfMuonParams(ctypes.Structure):
         ("reserve_sms", ctypes.c_int32),
         ("preconditioning", ctypes.c_int32),
         ("adaptive", ctypes.c_int32),
+        ("magma_tau", ctypes.c_float),
     ]
 
 
@@ -143,6 +147,8 @@ class RfAdamLeaf(ctypes.Structure):
         ("sr_seed_mu", ctypes.c_uint64),
         ("sr_seed_nu", ctypes.c_uint64),
         ("decay_mask", ctypes.c_void_p),
+        ("magma_score", ctypes.c_void_p),
+        ("magma_keep", ctypes.c_int32),
     ]
 
 
@@ -156,6 +162,9 @@ class RfAdamParams(ctypes.Structure):
         ("nesterov", ctypes.c_int32),
         ("lr", ctypes.c_float),
         ("max_ctas_per_sm", ctypes.c_int32),
+        ("magma_tau", ctypes.c_float),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -205,6 +214,7 @@ def load(path: str | None = None):
                                                  i32, i32, ctypes.c_float, i32, vp]
         lib.rf_muon_tail.argtypes = [ctypes.POINTER(RfTailLeaf), i32, ctypes.c_float, i32, vp]
         lib.rf_adamw_update.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(RfAdamParams), vp]
+        lib.rf_adamw_workspace_size.argtypes = [ctypes.POINTER(RfAdamLeaf), i32, ctypes.POINTER(sz)]
         lib.rf_apply_updates.argtypes = [ctypes.POINTER(RfApplyLeaf), i32, i32, vp]
         lib.rf_ipc_export.argtypes = [vp, ctypes.POINTER(RfIpcHandle), ctypes.POINTER(sz)]
         lib.rf_ipc_open.argtypes = [ctypes.POINTER(RfIpcHandle), ctypes.POINTER(vp)]

@@ -3,15 +3,20 @@
 
 from __future__ import annotations
 
+import ctypes
 from typing import Any, NamedTuple
 
 import torch
 
-from . import _lib
+from . import _lib, _runtime
 from .base import (
     AddDecayedWeightsState,
     GradientTransformation,
+    advance_key,
     decay_at,
+    init_magma_state,
+    magma_keeps,
+    validate_magma_args,
     MaskedState,
     ScaleByScheduleState,
     ScaleState,
@@ -57,14 +62,19 @@ def zeros_like_tree(params, dtype=torch.float32):
 
 
 def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float,
-             max_ctas_per_sm: int = 0, seeds=None) -> None:
+             max_ctas_per_sm: int = 0, seeds=None, magma=None, magma_tau: float = 2.0) -> None:
     """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype[, mask]);
     ``mask``: an optional uint8 tensor shaped like g (element-wise decay
-    mask); ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state."""
+    mask); ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state;
+    ``magma``: None, or per item (score tensor, keep) for Magma."""
     if not items:
         return
     lib = _lib.load()
     arr = (_lib.RfAdamLeaf * len(items))()
+    if magma is not None:
+        for i, (score, keep) in enumerate(magma):
+            arr[i].magma_score = score.data_ptr()
+            arr[i].magma_keep = int(keep)
     for i, item in enumerate(items):
         g, mu, nu, p, out, decay, rdt = item[:7]
         mask = item[7] if len(item) > 7 else None
@@ -84,7 +94,12 @@ def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: fl
         if seeds is not None:
             arr[i].sr_seed_mu, arr[i].sr_seed_nu = seeds[2 * i], seeds[2 * i + 1]
     prm = _lib.RfAdamParams(float(b1), float(b2), float(eps), float(eps_root), int(count), int(bool(nesterov)),
-                            float(lr), int(max_ctas_per_sm))
+                            float(lr), int(max_ctas_per_sm), float(magma_tau))
+    if magma is not None:
+        nbytes = ctypes.c_size_t()
+        _lib.check(lib.rf_adamw_workspace_size(arr, len(items), ctypes.byref(nbytes)))
+        ws = _runtime.workspace(items[0][0].device, nbytes.value)
+        prm.workspace, prm.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check(lib.rf_adamw_update(arr, len(items), prm,
                                    torch.cuda.current_stream(items[0][0].device).cuda_stream))
 
@@ -135,6 +150,17 @@ def _adam_items(updates, state, params, *, decay: float, decay_mask, decay_round
     return items, outs, treedef
 
 
+def _magma_items(updates, state, use_magma: bool, p: float, n_items: int):
+    """(per item (score, keep), key) for Magma, or (None, key)."""
+    if not use_magma:
+        return None, state.key
+    leaves = tree_flatten(updates, is_leaf=is_aux_leaf)[0]
+    scores = tree_flatten(state.magma_s, is_leaf=is_aux_leaf)[0]
+    pos = [i for i, g in enumerate(leaves) if not is_aux_leaf(g)]
+    keeps = magma_keeps(state.key, n_items, p)
+    return [(scores[i], k) for i, k in zip(pos, keeps)], state.key
+
+
 def wd_count(st) -> int:
     """Step count of an add_decayed_weights state (0 for a constant decay)."""
     inner = st.inner_state if isinstance(st, MaskedState) else st
@@ -163,17 +189,18 @@ def adam_seeds(items, key):
 def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, weight_decay=0.0,
                   weight_decay_mask=None, nesterov: bool = False, use_magma: bool = False, magma_p: float = 0.5,
                   magma_tau: float = 2.0, axis_name=None, key=None) -> GradientTransformation:
-    """adam.py:38-235 (no Magma): returns the Adam direction
+    """adam.py:38-235: returns the Adam direction
     m_hat / (sqrt(v_hat + eps_root) + eps), plus the in-transform decoupled
-    decay when ``params`` are given (adam.py:185-201)."""
+    decay when ``params`` are given (adam.py:185-201), then with ``use_magma``
+    the Magma factor keep * score per leaf (adam.py:204-215)."""
     if use_magma:
-        raise NotImplementedError("Magma masking is not on the B200 hot path")
+        validate_magma_args(magma_p, magma_tau)
     sdt = state_dtype(mu_dtype)
 
     def init_fn(params):
         # adam.py:98-112: both moments in mu_dtype (float32 by default).
-        return ScaleByAdamState(new_count(0), zeros_like_tree(params, sdt), zeros_like_tree(params, sdt), (),
-                                fresh_key(key))
+        return ScaleByAdamState(new_count(0), zeros_like_tree(params, sdt), zeros_like_tree(params, sdt),
+                                init_magma_state(params) if use_magma else (), fresh_key(key))
 
     def update_fn(updates, state, params=None):
         if has_nonzero_or_scheduled(weight_decay) and params is None:
@@ -187,9 +214,12 @@ def scale_by_adam(b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None, *, we
         wd_step, _ = decay_at(weight_decay, count)
         items, outs, treedef = _adam_items(updates, state, params, decay=wd_step, decay_mask=mask,
                                            decay_rounding_param=False)
+        magma, _ = _magma_items(updates, state, use_magma, magma_p, len(items))
         seeds, key_next = adam_seeds(items, state.key)
+        if use_magma and key_next is state.key:
+            key_next = advance_key(state.key)  # the Magma subkey splits the key (adam.py:128-131)
         run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=count, nesterov=nesterov, lr=-1.0,
-                 seeds=seeds)
+                 seeds=seeds, magma=magma, magma_tau=magma_tau)
         new_state = ScaleByAdamState(safe_increment(state.count), state.mu, state.nu, state.magma_s, key_next)
         return tree_unflatten(treedef, outs), new_state
 
@@ -204,14 +234,15 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
     (ScaleByAdamState, [AddDecayedWeightsState], ScaleState | ScaleByScheduleState)."""
     decay_on = has_nonzero_or_scheduled(weight_decay)
     if use_magma:
-        raise NotImplementedError("Magma masking is not on the B200 hot path")
+        validate_magma_args(magma_p, magma_tau)
     state_dtype(mu_dtype)  # validates
     scheduled = callable(weight_decay)
-    inner = scale_by_adam(b1, b2, eps, eps_root, mu_dtype, nesterov=nesterov, key=key)
+    inner = scale_by_adam(b1, b2, eps, eps_root, mu_dtype, nesterov=nesterov, use_magma=use_magma, magma_p=magma_p,
+                          magma_tau=magma_tau, key=key)
 
     def init_fn(params):
         states = [inner.init(params)]
-        if decay_on:
+        if decay_on and not use_magma:  # with Magma the decay is inside scale_by_adam (adam.py:385-401)
             wd_state = AddDecayedWeightsState(new_count(0)) if scheduled else AddDecayedWeightsState()
             states.append(MaskedState(wd_state) if weight_decay_mask is not None else wd_state)
         states.append(ScaleByScheduleState(new_count(0)) if callable(learning_rate) else ScaleState())
@@ -228,12 +259,21 @@ def adamw(learning_rate, b1=0.9, b2=0.999, eps=1e-8, eps_root=0.0, mu_dtype=None
         lr = resolve_scalar(learning_rate, host_count(lr_state.count)) if callable(learning_rate) else float(
             learning_rate)
         mask = resolve_mask(weight_decay_mask, params) if (decay_on and params is not None) else None
-        wd, weak = decay_at(weight_decay, host_count(wd_count(state[1]))) if decay_on else (0.0, True)
-        items, outs, treedef = _adam_items(updates, adam_state, params, decay=wd, decay_mask=mask,
-                                           decay_rounding_param=True, decay_weak=weak)
+        if use_magma:
+            # In-transform decay at the Adam count, float32 product, array masks.
+            wd, _ = decay_at(weight_decay, host_count(adam_state.count)) if decay_on else (0.0, True)
+            items, outs, treedef = _adam_items(updates, adam_state, params, decay=wd, decay_mask=mask,
+                                               decay_rounding_param=False)
+        else:
+            wd, weak = decay_at(weight_decay, host_count(wd_count(state[1]))) if decay_on else (0.0, True)
+            items, outs, treedef = _adam_items(updates, adam_state, params, decay=wd, decay_mask=mask,
+                                               decay_rounding_param=True, decay_weak=weak)
+        magma, _ = _magma_items(updates, adam_state, use_magma, magma_p, len(items))
         seeds, key_next = adam_seeds(items, adam_state.key)
+        if use_magma and key_next is adam_state.key:
+            key_next = advance_key(adam_state.key)
         run_adam(items, b1=b1, b2=b2, eps=eps, eps_root=eps_root, count=host_count(adam_state.count),
-                 nesterov=nesterov, lr=lr, seeds=seeds)
+                 nesterov=nesterov, lr=lr, seeds=seeds, magma=magma, magma_tau=magma_tau)
         new_adam = ScaleByAdamState(safe_increment(adam_state.count), adam_state.mu, adam_state.nu,
                                     adam_state.magma_s, key_next)
         new_lr = ScaleByScheduleState(safe_increment(lr_state.count)) if callable(learning_rate) else lr_state

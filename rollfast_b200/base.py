@@ -391,6 +391,42 @@ def sr_step_seeds(key, n: int) -> tuple[list, torch.Tensor]:
     return seeds, torch.tensor([(nk >> 32) & 0xFFFFFFFF, nk & 0xFFFFFFFF], dtype=torch.int64)
 
 
+def advance_key(key) -> torch.Tensor:
+    """The state key of the next step (the key sr_step_seeds returns)."""
+    return sr_step_seeds(key, 0)[1]
+
+
+_MAGMA_DOMAIN = 0x6A09E667F3BCC908
+
+
+def magma_keeps(key, n: int, p: float) -> list[int]:
+    """One Magma step's per-leaf Bernoulli(p) draws (magma.py:83, 122: a
+    subkey per leaf, ``bernoulli(subkey, p)``).  The reference draws from
+    JAX's Threefry stream; here each leaf's draw is a SplitMix64 output of a
+    stream derived from the state key, ``keep = u < p`` with
+    ``u = (x >> 11) * 2**-53`` uniform on [0, 1): the same distribution, a
+    different sequence."""
+    base = _splitmix64(key_seed(key) ^ _MAGMA_DOMAIN)
+    m = (1 << 64) - 1
+    return [int((_splitmix64((base + i) & m) >> 11) * (2.0 ** -53) < p) for i in range(n)]
+
+
+def init_magma_state(params):
+    """utils.py:64-69: a float32 score of 0.5 per (non-aux) leaf, on the
+    leaf's device (meta for meta leaves)."""
+    leaves, treedef = tree_flatten(params, is_leaf=is_aux_leaf)
+    return tree_unflatten(treedef, [x if is_aux_leaf(x) else torch.full((), 0.5, dtype=torch.float32, device=x.device)
+                                    for x in leaves])
+
+
+def validate_magma_args(p: float, tau: float) -> None:
+    """magma.py:8-13."""
+    if not 0.0 <= p <= 1.0:
+        raise ValueError(f"magma_p must be in [0, 1], got {p!r}.")
+    if tau <= 0.0:
+        raise ValueError(f"magma_tau must be positive, got {tau!r}.")
+
+
 def apply_updates(params, updates, key=None, stochastic: bool = True):
     """rollfast.utils.apply_updates (utils.py:648-708) on the
     ``rf_apply_updates`` kernel: ``p + u`` in float32, cast to the parameter

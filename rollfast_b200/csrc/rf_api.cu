@@ -102,6 +102,9 @@ struct LeafPlan {
   int64_t scale_index;  // first matrix in the scale array
   int mu_bf16;          // momentum stored as bfloat16 (stochastic rounding)
   uint64_t sr_seed;
+  float* magma_score;   // Magma score (device), null when off
+  int magma_keep;
+  int64_t magma_chunk;  // first Magma partial-sum chunk of this leaf
 };
 
 struct GroupPlan {
@@ -115,6 +118,8 @@ struct Plan {
   int64_t total_mats = 0;
   int64_t total_chunks = 0;
   size_t off_partials = 0, off_scale = 0, off_ns = 0, bytes = 0;
+  size_t off_magma = 0, off_factor = 0;  // Magma partial sums [chunks][3], per-leaf factors
+  int64_t magma_chunks = 0;
   size_t ns_bytes = 0;  // one region: max over sub-batches
   int regions = 1;      // 2 when pipelined on an aux stream
   int precision = RF_NS_F16;
@@ -136,6 +141,10 @@ static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan
   std::vector<std::vector<int>> members;
   for (size_t i = 0; i < P.leaves.size(); ++i) {
     LeafPlan& L = P.leaves[i];
+    if (L.magma_score) {
+      L.magma_chunk = P.magma_chunks;
+      P.magma_chunks += chunks_per_mat(L.batch * L.rows * L.cols);
+    }
     L.scale_index = P.total_mats;
     P.total_mats += L.batch;
     P.total_chunks += L.batch * chunks_per_mat(L.rows * L.cols);
@@ -183,7 +192,9 @@ static rf_status build_plan(const std::vector<LeafPlan>& in, int precision, Plan
   P.regions = regions;
   P.off_partials = 0;
   P.off_scale = align_up(size_t(P.total_chunks) * 4, 1024);
-  P.off_ns = P.off_scale + align_up(size_t(P.total_mats) * 4, 1024);
+  P.off_magma = P.off_scale + align_up(size_t(P.total_mats) * 4, 1024);
+  P.off_factor = P.off_magma + align_up(size_t(P.magma_chunks) * 12, 1024);
+  P.off_ns = P.off_factor + align_up(P.leaves.size() * 4, 1024);
   P.bytes = P.off_ns + size_t(regions) * P.ns_bytes;
   return RF_OK;
 }
@@ -243,6 +254,53 @@ static rf_status prepare_norms(const Plan& P, const std::vector<int>& ids, const
   return RF_OK;
 }
 
+// Magma for the leaves `ids` (magma.py:86-128): partial sums of <g, mu_t>,
+// |g|^2, |mu_t|^2 from the previous momentum (so this runs before the
+// momentum pass updates it), then each leaf's new score and factor.
+static rf_status magma_pass(const Plan& P, const std::vector<int>& ids, const MomentumCoeffs& mc, float tau,
+                            uint8_t* base, cudaStream_t st) {
+  float* partials = reinterpret_cast<float*>(base + P.off_magma);
+  float* factors = reinterpret_cast<float*>(base + P.off_factor);
+  std::vector<int> sel;
+  for (int i : ids)
+    if (P.leaves[i].magma_score) sel.push_back(i);
+  for (size_t s0 = 0; s0 < sel.size(); s0 += kMaxLeavesPerLaunch) {
+    MagmaDotLaunch D{};
+    MagmaFinLaunch F{};
+    D.s = mc.s;
+    D.beta = mc.beta;
+    F.tau = tau;
+    const int64_t first = P.leaves[sel[s0]].magma_chunk;
+    D.partials = partials + 3 * first;
+    F.partials = partials + 3 * first;
+    int64_t chunks = 0;
+    for (size_t k = s0; k < std::min(sel.size(), s0 + size_t(kMaxLeavesPerLaunch)); ++k) {
+      const LeafPlan& lp = P.leaves[sel[k]];
+      const int64_t n = lp.batch * lp.rows * lp.cols;
+      MagmaDotLeaf& d = D.leaf[D.n++];
+      d.g = lp.g;
+      d.mu = lp.mu;
+      d.n = n;
+      d.chunk_begin = chunks;
+      d.gdt = lp.gdt;
+      d.mu_bf16 = lp.mu_bf16;
+      d.vec_ok = (n % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.g) % 16 == 0) &&
+                 (reinterpret_cast<uintptr_t>(lp.mu) % 16 == 0);
+      MagmaFinLeaf& f = F.leaf[F.n++];
+      f.chunk_begin = chunks;
+      f.chunks = chunks_per_mat(n);
+      f.score = lp.magma_score;
+      f.factor = factors + sel[k];
+      f.keep = lp.magma_keep;
+      chunks += f.chunks;
+    }
+    D.total_chunks = chunks;
+    RF_TRY(launch_magma_dot(D, st));
+    RF_TRY(launch_magma_finalize(F, st));
+  }
+  return RF_OK;
+}
+
 // RAII set of events (host objects; no device memory).
 struct EventPool {
   std::vector<cudaEvent_t> ev;
@@ -266,7 +324,8 @@ struct EventPool {
 // GEMMs; workspace regions alternate, so preparing k+2 waits for k's GEMMs.
 static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const float* coeffs, int n_coeff_rows,
                               int ns_steps, float eps, int precond, int adaptive, int fuse_tail, float lr,
-                              int reserve_sms, void* ws, size_t ws_bytes, cudaStream_t st, cudaStream_t aux) {
+                              int reserve_sms, void* ws, size_t ws_bytes, cudaStream_t st, cudaStream_t aux,
+                              float magma_tau = 2.f) {
   if (P.leaves.empty()) return RF_OK;
   if (!ws || ws_bytes < P.bytes)
     return fail(RF_EINVAL, "workspace too small: need " + std::to_string(P.bytes) + " bytes, got " +
@@ -308,6 +367,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
 
       // ---- preparation: momentum, norms, operand load ----
       if (aux && k >= 2) cudaStreamWaitEvent(aux, done[k - 2], 0);  // region reuse
+      if (P.magma_chunks) RF_TRY(magma_pass(P, sub, mc, magma_tau, base, prep));
       RF_TRY(prepare_norms(P, sub, mc, partials, chunk_base, denom, eps, prep));
       chunk_base += sub_chunks;
 
@@ -359,6 +419,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         f.shape_scale = lp.shape_scale;
         f.decay = lp.decay;
         f.decay_dt = lp.decay_dt;
+        f.scale_dev = lp.magma_score ? reinterpret_cast<const float*>(base + P.off_factor) + li : nullptr;
         // Runs of 32 along the leaf's rows: length n (NS columns) for a
         // plain leaf, m (NS rows) for a transposed one.
         f.vec_ok = ((lp.transposed ? gp.m : gp.n) % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
@@ -477,6 +538,8 @@ static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vec
     p.decay_dt = l.decay_in_f32 ? RF_F32 : p.pdt;
     p.mu_bf16 = l.mu_dtype == RF_BF16;
     p.sr_seed = l.sr_seed;
+    p.magma_score = l.magma_score;
+    p.magma_keep = l.magma_keep ? 1 : 0;
     out.push_back(p);
   }
   return RF_OK;
@@ -613,6 +676,11 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   RF_TRY(build_plan(lp, p.precision, P, p.aux_stream ? 2 : 1));
   if (p.preconditioning < RF_PRECOND_FROBENIUS || p.preconditioning > RF_PRECOND_SCHATTEN)
     return fail(RF_EINVAL, "unknown preconditioning");
+  if (P.magma_chunks) {
+    if (!(p.magma_tau > 0.f)) return fail(RF_EINVAL, "magma_tau must be positive");
+    if (p.adaptive) return fail(RF_ENOTSUP, "Magma together with adaptive is not supported");
+    if (!p.fuse_tail) return fail(RF_ENOTSUP, "Magma needs the fused tail (fuse_tail = 1)");
+  }
   if (p.adaptive) {
     const MomentumCoeffs mc = momentum_coeffs(p);
     RF_TRY(run_pipeline(P, mc, p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 1, 0, 0.f, p.reserve_sms,
@@ -623,7 +691,7 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   return run_pipeline(P, momentum_coeffs(p), p.coeffs, p.n_coeff_rows, iters, p.eps, p.preconditioning, 0,
                       p.fuse_tail, p.lr,
                       p.reserve_sms, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
-                      static_cast<cudaStream_t>(p.aux_stream));
+                      static_cast<cudaStream_t>(p.aux_stream), p.magma_tau);
 }
 
 rf_status rf_muon_direction(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_muon_params* params,
@@ -787,11 +855,40 @@ rf_status rf_muon_tail(const rf_tail_leaf* leaves, int32_t n_leaves, float lr, i
   return RF_OK;
 }
 
+// Magma workspace of rf_adamw_update: [chunks][3] partial sums, then one
+// factor per leaf.
+static void adam_magma_layout(const rf_adam_leaf* leaves, int32_t n, int64_t* chunks, size_t* off_factor,
+                              size_t* bytes) {
+  int64_t c = 0;
+  for (int i = 0; i < n; ++i)
+    if (leaves[i].magma_score) c += ceil_div(leaves[i].n, kChunk);
+  *chunks = c;
+  *off_factor = align_up(size_t(c) * 12, 256);
+  *bytes = c ? *off_factor + align_up(size_t(n) * 4, 256) : 0;
+}
+
+rf_status rf_adamw_workspace_size(const rf_adam_leaf* leaves, int32_t n_leaves, size_t* bytes) {
+  if (!bytes) return fail(RF_EINVAL, "null output pointer");
+  if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
+  int64_t chunks = 0;
+  size_t off = 0;
+  adam_magma_layout(leaves, n_leaves, &chunks, &off, bytes);
+  return RF_OK;
+}
+
 rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf_adam_params* params,
                           void* stream) {
   if (!params) return fail(RF_EINVAL, "null params");
   if (n_leaves < 0 || (n_leaves > 0 && !leaves)) return fail(RF_EINVAL, "null leaf table");
   const rf_adam_params& p = *params;
+  int64_t magma_chunks = 0;
+  size_t off_factor = 0, magma_bytes = 0;
+  adam_magma_layout(leaves, n_leaves, &magma_chunks, &off_factor, &magma_bytes);
+  if (magma_chunks) {
+    if (!(p.magma_tau > 0.f)) return fail(RF_EINVAL, "magma_tau must be positive");
+    if (!p.workspace || p.workspace_bytes < magma_bytes)
+      return fail(RF_EINVAL, "Magma needs a workspace of " + std::to_string(magma_bytes) + " bytes");
+  }
   if (p.count < 0) return fail(RF_EINVAL, "count must be >= 0");
   if (p.max_ctas_per_sm < 0) return fail(RF_EINVAL, "max_ctas_per_sm must be >= 0");
   AdamCoeffs c{};
@@ -810,6 +907,51 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
   c.neg_lr = -p.lr;
   c.nesterov = p.nesterov;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* magma_partials = magma_chunks ? static_cast<float*>(p.workspace) : nullptr;
+  float* factors = magma_chunks ? reinterpret_cast<float*>(static_cast<uint8_t*>(p.workspace) + off_factor) : nullptr;
+  if (magma_chunks) {
+    // Scores and factors first (they read the previous first moment, which
+    // the AdamW kernel then updates in place): adam.py:204-215 with
+    // mu_t = (1 - b1) g + b1 mu.
+    std::vector<int> sel;
+    for (int i = 0; i < n_leaves; ++i)
+      if (leaves[i].magma_score) sel.push_back(i);
+    int64_t cursor = 0;
+    for (size_t s0 = 0; s0 < sel.size(); s0 += kMaxLeavesPerLaunch) {
+      MagmaDotLaunch D{};
+      MagmaFinLaunch F{};
+      D.s = c.one_minus_b1;
+      D.beta = c.b1;
+      D.partials = magma_partials + 3 * cursor;
+      F.partials = D.partials;
+      F.tau = p.magma_tau;
+      int64_t chunks = 0;
+      for (size_t k = s0; k < std::min(sel.size(), s0 + size_t(kMaxLeavesPerLaunch)); ++k) {
+        const rf_adam_leaf& l = leaves[sel[k]];
+        if (l.n > 0 && (!l.grad || !l.mu)) return fail(RF_EINVAL, "adam leaf: bad pointers");
+        MagmaDotLeaf& d = D.leaf[D.n++];
+        d.g = l.grad;
+        d.mu = l.mu;
+        d.n = l.n;
+        d.chunk_begin = chunks;
+        d.gdt = l.grad_dtype;
+        d.mu_bf16 = l.state_dtype == RF_BF16;
+        d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0);
+        MagmaFinLeaf& f = F.leaf[F.n++];
+        f.chunk_begin = chunks;
+        f.chunks = ceil_div(l.n, kChunk);
+        f.score = l.magma_score;
+        f.factor = factors + sel[k];
+        f.keep = l.magma_keep ? 1 : 0;
+        chunks += f.chunks;
+      }
+      D.total_chunks = chunks;
+      cursor += chunks;
+      RF_TRY(launch_magma_dot(D, st));
+      RF_TRY(launch_magma_finalize(F, st));
+    }
+  }
   for (int s = 0; s < n_leaves; s += kMaxLeavesPerLaunch) {
     AdamLaunch A{};
     A.c = c;
@@ -841,6 +983,7 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
       d.seed_mu = l.sr_seed_mu;
       d.seed_nu = l.sr_seed_nu;
       d.mask = l.decay != 0.f ? l.decay_mask : nullptr;
+      d.scale_dev = l.magma_score ? factors + i : nullptr;
       d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.nu) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.out) % 16 == 0) &&

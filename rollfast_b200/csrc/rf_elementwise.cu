@@ -436,6 +436,7 @@ __device__ __forceinline__ float adam_one(const AdamCoeffs& c, const AdamLeafDev
   const float nh = __fdiv_rn(nu, c.bc2);
   float u = __fdiv_rn(mh, __fadd_rn(__fsqrt_rn(__fadd_rn(nh, c.eps_root)), c.eps));
   if (decay_on) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, p));
+  if (L.scale_dev) u = __fmul_rn(*L.scale_dev, u);  // Magma: (keep * score) * u (magma.py:126-128)
   return __fmul_rn(c.neg_lr, u);
 }
 
@@ -490,6 +491,83 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
         st_from_float(L.out, L.odt, i, u);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Magma (magma.py:86-128).  k_magma_dot: per chunk of one leaf, the sums
+// <g, mu_t>, <g, g>, <mu_t, mu_t> in float32 with mu_t recomputed exactly as
+// the momentum kernels form it.  k_magma_finalize: one CTA per leaf sums its
+// chunks in a fixed order, then cos = clip(nan_to_num(dot / max(|g| |mu_t|,
+// 1e-12)), -1, 1), score <- 0.9 score + 0.1 sigmoid(cos / tau), factor =
+// keep * score (the leaf's Bernoulli draw times its new score).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kEwThreads) k_magma_dot(const __grid_constant__ MagmaDotLaunch P) {
+  __shared__ int64_t s_begin[kMaxLeavesPerLaunch];
+  __shared__ float red[32];
+  for (int i = threadIdx.x; i < P.n; i += blockDim.x) s_begin[i] = P.leaf[i].chunk_begin;
+  __syncthreads();
+  for (int64_t chunk = blockIdx.x; chunk < P.total_chunks; chunk += gridDim.x) {
+    const int li = find_leaf(s_begin, P.n, chunk);
+    const MagmaDotLeaf& L = P.leaf[li];
+    const int64_t lo = (chunk - L.chunk_begin) * kChunk;
+    const int64_t hi = (lo + kChunk < L.n ? lo + kChunk : L.n);
+    float gm = 0.f, gg = 0.f, mm = 0.f;
+    if (L.vec_ok) {
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float g[8], m[8];
+        ld8(L.g, L.gdt, i, g);
+        ld8(L.mu, L.mu_bf16 ? RF_BF16 : RF_F32, i, m);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float mt = __fadd_rn(__fmul_rn(P.s, g[k]), __fmul_rn(P.beta, m[k]));
+          gm = fmaf(g[k], mt, gm);
+          gg = fmaf(g[k], g[k], gg);
+          mm = fmaf(mt, mt, mm);
+        }
+      }
+    } else {
+      for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float g = ld_as_float(L.g, L.gdt, i);
+        const float m = ld_as_float(L.mu, L.mu_bf16 ? RF_BF16 : RF_F32, i);
+        const float mt = __fadd_rn(__fmul_rn(P.s, g), __fmul_rn(P.beta, m));
+        gm = fmaf(g, mt, gm);
+        gg = fmaf(g, g, gg);
+        mm = fmaf(mt, mt, mm);
+      }
+    }
+    const float a = block_sum(gm, red);
+    const float b = block_sum(gg, red);
+    const float c = block_sum(mm, red);
+    if (threadIdx.x == 0) {
+      P.partials[3 * chunk] = a;
+      P.partials[3 * chunk + 1] = b;
+      P.partials[3 * chunk + 2] = c;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kEwThreads) k_magma_finalize(const __grid_constant__ MagmaFinLaunch P) {
+  __shared__ float red[32];
+  for (int li = blockIdx.x; li < P.n; li += gridDim.x) {
+    const MagmaFinLeaf& L = P.leaf[li];
+    float s3[3] = {0.f, 0.f, 0.f};
+    for (int j = 0; j < 3; ++j) {
+      float acc = 0.f;
+      for (int64_t c = threadIdx.x; c < L.chunks; c += blockDim.x) acc += P.partials[3 * (L.chunk_begin + c) + j];
+      s3[j] = block_sum(acc, red);
+    }
+    if (threadIdx.x == 0) {
+      const float denom = fmaxf(__fmul_rn(__fsqrt_rn(s3[1]), __fsqrt_rn(s3[2])), 1e-12f);
+      float cs = __fdiv_rn(s3[0], denom);
+      if (cs != cs) cs = 0.f;  // nan_to_num(nan=0); +-inf are clipped below
+      cs = fminf(fmaxf(cs, -1.f), 1.f);
+      const float st = 1.f / (1.f + expf(-__fdiv_rn(cs, P.tau)));  // sigmoid(cos / tau)
+      const float s_new = __fadd_rn(__fmul_rn(0.9f, *L.score), __fmul_rn(0.1f, st));
+      *L.score = s_new;
+      *L.factor = __fmul_rn(L.keep ? 1.f : 0.f, s_new);
+    }
+    __syncthreads();
   }
 }
 
@@ -648,6 +726,18 @@ __global__ void __launch_bounds__(kEwThreads) k_apply(const __grid_constant__ Ap
 static int ew_grid(int64_t work, int ctas_per_sm = 8) {
   const int64_t cap = int64_t(num_sms()) * (ctas_per_sm > 0 ? ctas_per_sm : 8);
   return int(work < cap ? (work > 0 ? work : 1) : cap);
+}
+
+rf_status launch_magma_dot(const MagmaDotLaunch& P, cudaStream_t st) {
+  if (P.total_chunks == 0) return RF_OK;
+  k_magma_dot<<<ew_grid(P.total_chunks), kEwThreads, 0, st>>>(P);
+  return check_launch("k_magma_dot");
+}
+
+rf_status launch_magma_finalize(const MagmaFinLaunch& P, cudaStream_t st) {
+  if (P.n == 0) return RF_OK;
+  k_magma_finalize<<<P.n, kEwThreads, 0, st>>>(P);
+  return check_launch("k_magma_finalize");
 }
 
 rf_status launch_momentum_sumsq(const MomentumLaunch& P, int gdt, cudaStream_t st) {

@@ -96,7 +96,8 @@ struct AdamLeafDev {
   float decay;
   int32_t sdt;     // moment storage dtype: RF_F32, or RF_BF16 (stochastic rounding)
   uint64_t seed_mu, seed_nu;
-  const uint8_t* mask;  // optional element-wise decay mask
+  const uint8_t* mask;     // optional element-wise decay mask
+  const float* scale_dev;  // optional device factor applied after the decay (Magma: keep * score)
 };
 struct AdamLaunch {
   AdamLeafDev leaf[kMaxLeavesPerLaunch];
@@ -161,6 +162,7 @@ struct FinalLeaf {
   int32_t vec_ok;  // out / p 16-byte aligned and the leaf's row length % 8 == 0: vector epilogue
   float shape_scale, decay;
   int32_t decay_dt;  // dtype decay * p is rounded to (the parameter dtype, or RF_F32)
+  const float* scale_dev;  // optional device factor applied after the decay (Magma: keep * score)
 };
 
 struct NsGemmArgs {
@@ -226,6 +228,38 @@ struct ApplyLaunch {
   int stochastic;
 };
 rf_status launch_apply(const ApplyLaunch& P, cudaStream_t st);
+
+// Magma (src/rollfast/optim/magma.py:16-132): per leaf, partial sums over
+// chunks of <g, mu_t>, |g|^2, |mu_t|^2 with mu_t = s g + beta mu_{t-1}
+// recomputed from the previous state, then one fixed-order reduction per leaf
+// giving the score EMA and the update factor keep * score.
+struct MagmaDotLeaf {
+  const void* g;
+  const void* mu;      // previous first moment (float32, or bfloat16 storage)
+  int64_t n, chunk_begin;
+  int32_t gdt, mu_bf16, vec_ok;
+};
+struct MagmaDotLaunch {
+  MagmaDotLeaf leaf[kMaxLeavesPerLaunch];
+  int n;
+  int64_t total_chunks;
+  float s, beta;       // mu_t = s * g + beta * mu_{t-1}
+  float* partials;     // [total_chunks][3]
+};
+struct MagmaFinLeaf {
+  int64_t chunk_begin, chunks;
+  float* score;        // the leaf's score, read and updated in place
+  float* factor;       // out: keep * new score
+  int32_t keep;
+};
+struct MagmaFinLaunch {
+  MagmaFinLeaf leaf[kMaxLeavesPerLaunch];
+  int n;
+  float tau;
+  const float* partials;
+};
+rf_status launch_magma_dot(const MagmaDotLaunch& P, cudaStream_t st);
+rf_status launch_magma_finalize(const MagmaFinLaunch& P, cudaStream_t st);
 rf_status launch_adaptive_finalize(const AdaptiveLaunch& P, float* ip, cudaStream_t st);
 
 // Preconditioning variants (rf_precond.cu).  Reads A~ = sa X_F X_F^T of one
@@ -281,6 +315,7 @@ __device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf
   if (a.fuse_tail) {
     v = __fmul_rn(o, L.shape_scale);
     if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.decay_dt, L.decay, ld_as_float(L.p, L.p_dtype, idx)));
+    if (L.scale_dev) v = __fmul_rn(*L.scale_dev, v);
     v = __fmul_rn(a.neg_lr, v);
   }
   st_from_float(L.out, L.out_dtype, idx, v);
@@ -325,10 +360,12 @@ __device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const Fin
         }
       }
     }
+    const float fac = L.scale_dev ? *L.scale_dev : 1.f;
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       float u = __fmul_rn(v[k], L.shape_scale);
       if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, pv[k]));
+      if (L.scale_dev) u = __fmul_rn(fac, u);
       v[k] = __fmul_rn(a.neg_lr, u);
     }
   }

@@ -22,6 +22,7 @@ import torch
 from . import _lib, _runtime
 from .adam import (
     ScaleByAdamState,
+    _elementwise_mask,
     adam_seeds,
     adamw,
     bump_wd_state,
@@ -40,11 +41,14 @@ from .base import (
     ScaleByScheduleState,
     ScaleState,
     add_decayed_weights,
+    advance_key,
     chain,
     decay_at,
     has_nonzero_or_scheduled,
     host_count,
     init_empty_state,
+    init_magma_state,
+    magma_keeps,
     new_count,
     partition,
     resolve_mask,
@@ -59,6 +63,7 @@ from .base import (
     state_dtype,
     stream_handle,
     validate_beta,
+    validate_magma_args,
     validate_positive,
 )
 from .dimension_numbers import (
@@ -179,7 +184,9 @@ def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str, allow_meta:
     return out
 
 
-def _leaf_table(ml: list, scales, decays, decay_f32=None):
+def _leaf_table(ml: list, scales, decays, decay_f32=None, magma=None):
+    """``magma``: None, or (scores, keeps) per leaf (device score tensors and
+    this step's Bernoulli draws)."""
     arr = (_lib.RfMuonLeaf * max(1, len(ml)))()
     for i, L in enumerate(ml):
         b, r, c = L.layout.flat_shape
@@ -198,6 +205,9 @@ def _leaf_table(ml: list, scales, decays, decay_f32=None):
         e.mu_dtype = rf_dtype(L.mu)
         e.sr_seed = L.seed
         e.decay_in_f32 = int(bool(decay_f32[i])) if decay_f32 is not None else 0
+        if magma is not None:
+            e.magma_score = magma[0][i].data_ptr()
+            e.magma_keep = int(magma[1][i])
     return arr
 
 
@@ -212,7 +222,7 @@ def _seed_leaves(ml: list, key):
 
 
 def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps, lr, fuse_tail, reserve_sms=0,
-                 preconditioning: str = "frobenius", adaptive: bool = False):
+                 preconditioning: str = "frobenius", adaptive: bool = False, magma_tau: float = 2.0):
     cbuf, rows = coeff_buffer(ns_coeffs)
     prm = _lib.RfMuonParams()
     prm.beta = float(beta)
@@ -230,6 +240,7 @@ def _muon_params(*, beta, eps, count, nesterov, accumulator, ns_coeffs, ns_steps
     prm.reserve_sms = int(reserve_sms)
     prm.preconditioning = _lib.PRECONDITIONING_CODES[preconditioning]
     prm.adaptive = int(bool(adaptive))
+    prm.magma_tau = float(magma_tau)
     return prm, cbuf
 
 
@@ -246,10 +257,10 @@ def run_muon_table(arr, n: int, prm, dev: torch.device) -> None:
     _lib.check(lib.rf_muon_update(arr, n, ctypes.byref(prm), ws.data_ptr(), ws.numel(), main.cuda_stream))
 
 
-def _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32=None):
+def _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32=None, magma=None):
     if not ml:
         return
-    run_muon_table(_leaf_table(ml, scales, decays, decay_f32), len(ml), prm, ml[0].g.device)
+    run_muon_table(_leaf_table(ml, scales, decays, decay_f32, magma), len(ml), prm, ml[0].g.device)
     del cbuf
 
 
@@ -304,8 +315,11 @@ _resolve_ns_coeffs = resolve_ns_coeffs
 
 
 def _check_supported(*, adaptive, preconditioning, use_magma, mu_dtype, orthogonalize_fn):
-    if use_magma:
-        raise NotImplementedError("Magma masking is not on the B200 hot path")
+    if use_magma and adaptive:
+        raise NotImplementedError("use_magma together with adaptive=True is not supported")
+    if use_magma and orthogonalize_fn is not orthogonalize_via_newton_schulz:
+        raise NotImplementedError("use_magma with a custom orthogonalize_fn is not supported (the Magma factor is "
+                                  "applied in the fused Newton-Schulz epilogue)")
     if adaptive and orthogonalize_fn is not orthogonalize_via_newton_schulz:
         raise NotImplementedError("adaptive=True with a custom orthogonalize_fn is not supported "
                                   "(the default Newton-Schulz path computes <mu_hat, O> on the GPU)")
@@ -334,13 +348,17 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
             "Use `use_magma=True` or chain `optax.add_decayed_weights` separately."
         )
     _validate_accumulator(momentum_accumulator)
+    if use_magma:
+        validate_magma_args(magma_p, magma_tau)
     _check_supported(adaptive=adaptive, preconditioning=preconditioning, use_magma=use_magma, mu_dtype=mu_dtype,
                      orthogonalize_fn=orthogonalize_fn)
 
     def init_fn(params):
-        # muon.py:207-223: momentum in mu_dtype (float32 by default).
+        # muon.py:207-223: momentum in mu_dtype (float32 by default), Magma
+        # scores of 0.5 per leaf when use_magma.
         return MuonState(new_count(0), zeros_like_tree(params, state_dtype(mu_dtype)),
-                         resolve_ns_coeffs(ns_coeffs, ns_steps), (), fresh_key(key))
+                         resolve_ns_coeffs(ns_coeffs, ns_steps), init_magma_state(params) if use_magma else (),
+                         fresh_key(key))
 
     def update_fn(updates, state, params=None):
         dim_nums = _resolve_update_dimension_numbers(weight_dimension_numbers, params=params, updates=updates,
@@ -351,14 +369,46 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
             _validate_matrix_operand(u, d, "scale_by_muon")
         mus = tree_flatten(state.mu, is_leaf=is_aux_leaf)[0]
         count = host_count(state.count)
-        ml = _gather_muon_leaves(leaves, mus, None, specs, "scale_by_muon")
+        decay_on = use_magma and has_nonzero_or_scheduled(weight_decay)
+        if decay_on and params is None:
+            raise ValueError(
+                "`params` must be provided to `scale_by_muon.update` when `weight_decay` is nonzero or scheduled."
+            )
+        ps = tree_flatten(params, is_leaf=is_aux_leaf)[0] if decay_on else None
+        ml = _gather_muon_leaves(leaves, mus, ps, specs, "scale_by_muon")
+        keeps = magma_keeps(state.key, len(ml), magma_p) if use_magma else None
         ml, key_next = _seed_leaves(ml, state.key)
+        if use_magma and key_next is state.key:
+            key_next = advance_key(state.key)  # utils.py:545-562: the Magma subkey splits the key
+        # Shape scaling (shape_updates, muon.py:285-290), in-transform decay
+        # (use_magma, 297-304: wd at the state count, float32 product) and the
+        # Magma factor (309-322) all run in the fused final epilogue; lr = -1
+        # leaves the update unscaled.
+        fused = use_magma or shape_updates
+        ones, zeros = [1.0] * len(ml), [0.0] * len(ml)
+        scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml] if shape_updates else ones
+        decays, decay_f32 = list(zeros), [False] * len(ml)
+        if decay_on:
+            wd_step, _ = decay_at(weight_decay, count)
+            mask_tree = resolve_mask(weight_decay_mask, params)
+            masks = (tree_flatten(mask_tree, is_leaf=is_aux_leaf)[0] if mask_tree is not None
+                     else [True] * len(leaves))
+            for j, L in enumerate(ml):
+                m = masks[L.pos]
+                if not isinstance(m, bool) and getattr(m, "ndim", 0) > 0:
+                    raise NotImplementedError("element-wise weight-decay masks on Muon leaves with use_magma")
+                if bool(m) and L.p is not None:
+                    decays[j], decay_f32[j] = float(wd_step), True
+        magma = None
+        if use_magma:
+            scores = tree_flatten(state.magma_s, is_leaf=is_aux_leaf)[0]
+            magma = ([scores[L.pos] for L in ml], keeps)
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=count, nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=state.ns_coeffs, ns_steps=ns_steps,
-                                 lr=0.0, fuse_tail=0, preconditioning=preconditioning, adaptive=adaptive)
-        ones, zeros = [1.0] * len(ml), [0.0] * len(ml)
+                                 lr=-1.0 if fused else 0.0, fuse_tail=int(fused), preconditioning=preconditioning,
+                                 adaptive=adaptive, magma_tau=magma_tau)
         if orthogonalize_fn is orthogonalize_via_newton_schulz:
-            _run_muon_update(ml, prm, cbuf, ones, zeros)
+            _run_muon_update(ml, prm, cbuf, scales if fused else ones, decays, decay_f32, magma)
             outs = _finish_leaves(ml)
         else:
             # Caller-supplied hook: materialise the direction (mu_hat), then
@@ -369,6 +419,10 @@ def scale_by_muon(ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps=1e-8,
             dirs = _finish_leaves(ml)
             outs = [orthogonalize_fn(d, state.ns_coeffs, ns_steps, preconditioning, eps, L.spec)
                     for d, L in zip(dirs, ml)]
+            if shape_updates:  # muon.py:285-290 on the hook's output
+                scaled = [torch.empty_like(o) for o in outs]
+                run_tail([(o.contiguous(), None, s, sc, 0.0) for o, s, sc in zip(outs, scaled, scales)], -1.0)
+                outs = scaled
         full = list(leaves)
         for L, o in zip(ml, outs):
             full[L.pos] = o
@@ -470,18 +524,36 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         ctx = distributed.current()
         sharded = ctx is not None and ctx.world_size > 1
         owned_only = sharded and ctx.updates == "owned"
+        if use_magma and sharded:
+            raise NotImplementedError("use_magma with the sharded multi-GPU update is not supported")
         ml = _gather_muon_leaves(muon_leaves, mus, ps, muon_specs, "scale_by_muon", allow_meta=owned_only)
+        mkeeps = magma_keeps(muon_st.key, len(ml), magma_p) if use_magma else None
         ml, muon_key_next = _seed_leaves(ml, muon_st.key)
+        if use_magma and muon_key_next is muon_st.key:
+            muon_key_next = advance_key(muon_st.key)
         scales = [shape_factor(L.shape, L.spec, consistent_rms) for L in ml]
-        # add_decayed_weights of each branch: a constant, or a schedule at the
-        # transform's own count (its state is mstate[0][2] / astate[1]).
-        mwd, mweak = decay_at(weight_decay, wd_count(mstate[0][2])) if muon_wd_on else (0.0, True)
-        awd, aweak = decay_at(eff_adam_wd, wd_count(astate[1])) if adam_wd_on else (0.0, True)
+        if use_magma:
+            # Decay inside scale_by_muon / scale_by_adam (muon.py:297-304,
+            # adam.py:185-201): at each branch's state count, float32 product.
+            mwd, mweak = (decay_at(weight_decay, host_count(muon_st.count))[0], False) if muon_wd_on else (0.0, True)
+            awd, aweak = (decay_at(eff_adam_wd, host_count(adam_st.count))[0], False) if adam_wd_on else (0.0, True)
+        else:
+            # add_decayed_weights of each branch: a constant, or a schedule at
+            # the transform's own count (its state is mstate[0][2] / astate[1]).
+            mwd, mweak = decay_at(weight_decay, wd_count(mstate[0][2])) if muon_wd_on else (0.0, True)
+            awd, aweak = decay_at(eff_adam_wd, wd_count(astate[1])) if adam_wd_on else (0.0, True)
         decays, decay_f32 = [], []
         for L in ml:
-            on = muon_wd_on and bool(masks[L.pos]) and L.p is not None
+            m = masks[L.pos]
+            if use_magma and not isinstance(m, bool) and getattr(m, "ndim", 0) > 0:
+                raise NotImplementedError("element-wise weight-decay masks on Muon leaves with use_magma")
+            on = muon_wd_on and bool(m) and L.p is not None
             decays.append((round_to_dtype(mwd, L.p.dtype) if mweak else mwd) if on else 0.0)
             decay_f32.append(on and not mweak)
+        mmagma = None
+        if use_magma:
+            mscores = tree_flatten(muon_st.magma_s, is_leaf=is_aux_leaf)[0]
+            mmagma = ([mscores[L.pos] for L in ml], mkeeps)
         # AdamW fallback leaves (their `out` is allocated below unless the
         # sharded owner-side path writes them into its update arena).
         a_items, a_pos = [], []
@@ -495,23 +567,32 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             if g.dtype.is_complex:
                 raise NotImplementedError("complex leaves are not on the B200 hot path")
             p = ps[i]
-            on = adam_wd_on and bool(masks[i]) and p is not None and not is_aux_leaf(p)
+            m = masks[i]
+            elementwise = use_magma and not isinstance(m, bool) and getattr(m, "ndim", 0) > 0
+            on = adam_wd_on and (elementwise or bool(m)) and p is not None and not is_aux_leaf(p)
             if on:
                 a_items.append((g.contiguous(), amus[i], anus[i], p.contiguous(), None,
                                 round_to_dtype(awd, p.dtype) if aweak else awd,
-                                rf_dtype(p) if aweak else _lib.RF_F32))
+                                rf_dtype(p) if aweak else _lib.RF_F32,
+                                _elementwise_mask(m, g) if elementwise else None))
             else:
                 a_items.append((g.contiguous(), amus[i], anus[i], None, None, 0.0, _lib.RF_F32))
             a_pos.append(i)
+        akeeps = magma_keeps(adam_st.key, len(a_items), magma_p) if use_magma else None
         a_seeds, adam_key_next = adam_seeds(a_items, adam_st.key)
+        if use_magma and adam_key_next is adam_st.key:
+            adam_key_next = advance_key(adam_st.key)
         adam_kw = dict(b1=adam_b1, b2=adam_b2, eps=adam_eps, eps_root=adam_eps_root,
                        count=host_count(adam_st.count), nesterov=nesterov, lr=alr)
+        if use_magma:
+            ascores = tree_flatten(adam_st.magma_s, is_leaf=is_aux_leaf)[0]
+            adam_kw.update(magma=[(ascores[i], k) for i, k in zip(a_pos, akeeps)], magma_tau=magma_tau)
 
         prm, cbuf = _muon_params(beta=beta, eps=eps, count=host_count(muon_st.count), nesterov=nesterov,
                                  accumulator=momentum_accumulator, ns_coeffs=muon_st.ns_coeffs,
                                  ns_steps=ns_steps, lr=lr, fuse_tail=1,
                                  reserve_sms=ctx.reserve_sms if sharded else 0,
-                                 preconditioning=preconditioning, adaptive=adaptive)
+                                 preconditioning=preconditioning, adaptive=adaptive, magma_tau=magma_tau)
         res = None
         if owned_only:
             res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds)
@@ -526,7 +607,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             if sharded:
                 outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32)
             else:
-                _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32)
+                _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32, mmagma)
                 outs = _finish_leaves(ml)
             a_outs = [torch.empty(it[0].shape, dtype=torch.float32, device=it[0].device) for it in a_items]
             a_items = [(*it[:4], o, *it[5:]) for it, o in zip(a_items, a_outs)]

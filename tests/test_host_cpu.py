@@ -150,8 +150,14 @@ def test_adamw_rejects_negative_weight_decay():
 
 
 def test_unsupported_options_fail_loudly():
-    with pytest.raises(NotImplementedError):
-        rf.scale_by_muon(use_magma=True)
+    with pytest.raises(NotImplementedError, match="adaptive"):
+        rf.scale_by_muon(use_magma=True, adaptive=True)
+    with pytest.raises(NotImplementedError, match="orthogonalize_fn"):
+        rf.scale_by_muon(use_magma=True, orthogonalize_fn=lambda x, *a: x)
+    with pytest.raises(ValueError, match="magma_p"):
+        rf.scale_by_muon(use_magma=True, magma_p=1.5)  # magma.py:8-13
+    with pytest.raises(ValueError, match="magma_tau"):
+        rf.adamw(learning_rate=0.1, use_magma=True, magma_tau=0.0)
     with pytest.raises(ValueError, match="Unknown preconditioning"):
         rf.scale_by_muon(preconditioning="nuclear")
     with pytest.raises(NotImplementedError, match="adaptive"):
@@ -361,3 +367,21 @@ def test_in_transform_decay_oracle_masks_elementwise():
     np.testing.assert_array_equal(O.in_transform_decay(u, p, 0.5, np.array([[True, False]])),
                                   [[6.0, 2.0], [18.0, 4.0]])  # broadcast row mask
     np.testing.assert_array_equal(O.in_transform_decay(u, p, 0.5, False), u)
+
+
+def test_magma_state_and_draws():
+    """Magma state: a 0.5 float32 score per leaf (utils.py:64-69); the per-leaf
+    Bernoulli(p) draws are deterministic in the state key and have mean p."""
+    from rollfast_b200.base import magma_keeps
+
+    params = {"w": torch.zeros(8, 16), "b": torch.zeros(16)}
+    st = rf.muon(learning_rate=0.1, use_magma=True).init(params)
+    ms = st.inner_states["muon"].inner_state[0][0].magma_s
+    assert float(ms["w"]) == 0.5 and ms["w"].dtype == torch.float32
+    ast = st.inner_states["adam"].inner_state[0].magma_s
+    assert float(ast["b"]) == 0.5
+    k = torch.tensor([0, 42])
+    draws = magma_keeps(k, 20000, 0.3)
+    assert draws == magma_keeps(k, 20000, 0.3)
+    assert abs(sum(draws) / len(draws) - 0.3) < 0.015
+    assert set(magma_keeps(k, 100, 0.0)) == {0} and set(magma_keeps(k, 100, 1.0)) == {1}
