@@ -471,6 +471,9 @@ def main():
     ap.add_argument("--adaptive", action="store_true")
     ap.add_argument("--mu-dtype", default="float32", choices=["float32", "bfloat16"])
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--apply-updates", action="store_true",
+                    help="time update_and_apply (the parameter apply fused into the update, bf16 stochastic "
+                         "rounding, in place) instead of the update alone")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -554,9 +557,18 @@ def main():
     # Like a training loop, each step's updates are dropped (applied) before
     # the next step: holding two update trees (2 x 30 GiB) beside the state
     # and two gradient sets would leave little of the 178 GiB free.
+    apply_key = torch.tensor([0, 7])
+
+    def one_step(i, state):
+        if args.apply_updates:  # new parameters written in place; no update tree
+            _, state = rf.update_and_apply(tx, grad_sets[i % 2], state, params, apply_key, stochastic=True,
+                                           inplace=True)
+            return None, state
+        return tx.update(grad_sets[i % 2], state, params)
+
     for i in range(args.warmup):
         upd = None
-        upd, state = tx.update(grad_sets[i % 2], state, params)
+        upd, state = one_step(i, state)
     barrier()
 
     launches0 = _lib.kernel_launch_count()
@@ -567,7 +579,7 @@ def main():
         start.record()
         for i in range(args.steps):
             upd = None
-            upd, state = tx.update(grad_sets[i % 2], state, params)
+            upd, state = one_step(i, state)
         stop.record()
         barrier()
     prof = _lib.profile_end()
@@ -589,7 +601,7 @@ def main():
 
     # ---- e2e through host buffers (pinned grads H2D + updates D2H) ----------
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not args.apply_updates:
         try:
             e2e = run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist)
         except (RuntimeError, MemoryError) as exc:  # host RAM for pinned buffers
@@ -632,7 +644,8 @@ def main():
             "dtype": f"{args.precision} NS operands, fp32 accumulate/state, bf16 params+grads",
             "data": "synthetic: N(0,1) bf16 grads (2 seeded sets), N(0,0.02) bf16 params",
             "config": {"workload": workload
-                       + "".join(f"+{k}={v if k != 'mu_dtype' else args.mu_dtype}" for k, v in variant.items()),
+                       + "".join(f"+{k}={v if k != 'mu_dtype' else args.mu_dtype}" for k, v in variant.items())
+                       + ("+update_and_apply" if args.apply_updates else ""),
                        "baseline_config": baseline_cfg,
                        "model": model,
                        "muon_leaves": len(muon_matrix_shapes(shapes)),

@@ -87,6 +87,14 @@ typedef struct rf_muon_leaf {
    * magma_keep * score after the decay and before the learning rate. */
   float* magma_score;
   int32_t magma_keep;
+  /* Fused parameter apply (utils.py:648-708; needs fuse_tail and param):
+   * 0: `out` receives the update; 1: `out` (param_dtype, may alias param)
+   * receives the new parameter p + u, rounded to nearest even; 2: the same
+   * with bfloat16 stochastic rounding (noise of element i of apply_seed's
+   * SplitMix64 stream, as rf_apply_updates draws it for a leaf with that
+   * seed).  Saves writing the float32 update and reading it back. */
+  int32_t apply_mode;
+  uint64_t apply_seed;
 } rf_muon_leaf;
 
 /* Newton-Schulz preconditioning (orthogonalization.py:24, 153-176, 233-250). */
@@ -217,6 +225,8 @@ typedef struct rf_adam_leaf {
    * rf_adam_params. */
   float* magma_score;
   int32_t magma_keep;
+  int32_t apply_mode;   /* as in rf_muon_leaf (out in param_dtype) */
+  uint64_t apply_seed;
 } rf_adam_leaf;
 typedef struct rf_adam_params {
   /* b1, b2 as the caller's double-precision scalars: the reference forms

@@ -12,7 +12,7 @@ Leaves are CUDA ``torch.Tensor`` buffers; the compute runs in
 from . import distributed
 from ._runtime import set_ns_precision
 from .adam import ScaleByAdamState, adamw, scale_by_adam
-from .base import GradientTransformation, apply_updates
+from .base import GradientTransformation, apply_updates, update_and_apply
 from .dimension_numbers import MatrixDimensionNumbers, MuonDimensionNumbers, WeightDimNumOrFn
 from .muon import MuonState, muon, scale_by_muon, scale_by_muon_shape, scale_by_shape
 from .orthogonalization import (
@@ -55,4 +55,5 @@ __all__ = [
     "scale_by_muon_shape",
     "scale_by_shape",
     "set_ns_precision",
+    "update_and_apply",
 ]

@@ -91,6 +91,8 @@ class RfMuonLeaf(ctypes.Structure):
         ("decay_in_f32", ctypes.c_int32),
         ("magma_score", ctypes.c_void_p),
         ("magma_keep", ctypes.c_int32),
+        ("apply_mode", ctypes.c_int32),
+        ("apply_seed", ctypes.c_uint64),
     ]
 
 
@@ -149,6 +151,8 @@ class RfAdamLeaf(ctypes.Structure):
         ("decay_mask", ctypes.c_void_p),
         ("magma_score", ctypes.c_void_p),
         ("magma_keep", ctypes.c_int32),
+        ("apply_mode", ctypes.c_int32),
+        ("apply_seed", ctypes.c_uint64),
     ]
 
 

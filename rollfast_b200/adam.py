@@ -62,11 +62,13 @@ def zeros_like_tree(params, dtype=torch.float32):
 
 
 def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: float,
-             max_ctas_per_sm: int = 0, seeds=None, magma=None, magma_tau: float = 2.0) -> None:
+             max_ctas_per_sm: int = 0, seeds=None, magma=None, magma_tau: float = 2.0, apply=None) -> None:
     """items: (g, mu, nu, p_or_None, out, decay, decay_rounding_dtype[, mask]);
     ``mask``: an optional uint8 tensor shaped like g (element-wise decay
     mask); ``seeds``: two noise seeds per item (mu, nu) for bfloat16 state;
-    ``magma``: None, or per item (score tensor, keep) for Magma."""
+    ``magma``: None, or per item (score tensor, keep) for Magma; ``apply``:
+    None, or per item (mode, seed) of the fused parameter apply (``out`` then
+    receives the new parameter, in the parameter dtype)."""
     if not items:
         return
     lib = _lib.load()
@@ -75,6 +77,9 @@ def run_adam(items, *, b1, b2, eps, eps_root, count: int, nesterov: bool, lr: fl
         for i, (score, keep) in enumerate(magma):
             arr[i].magma_score = score.data_ptr()
             arr[i].magma_keep = int(keep)
+    if apply is not None:
+        for i, (mode, seed) in enumerate(apply):
+            arr[i].apply_mode, arr[i].apply_seed = int(mode), int(seed)
     for i, item in enumerate(items):
         g, mu, nu, p, out, decay, rdt = item[:7]
         mask = item[7] if len(item) > 7 else None

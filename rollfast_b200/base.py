@@ -471,3 +471,30 @@ def apply_updates(params, updates, key=None, stochastic: bool = True):
         _lib.check(lib.rf_apply_updates(arr, len(items), int(bool(stochastic)),
                                         torch.cuda.current_stream(items[0][0].device).cuda_stream))
     return tree_unflatten(treedef, outs)
+
+
+def update_and_apply(tx: GradientTransformation, grads, state, params, key=None, stochastic: bool = True,
+                     inplace: bool = False):
+    """One optimizer step that returns new parameters: ``tx.update`` followed
+    by ``apply_updates`` (utils.py:648-708), i.e.
+    ``apply_updates(params, *tx.update(grads, state, params)[:1], key, stochastic)``
+    together with the new state.
+
+    For ``rollfast_b200.muon(...)`` on one GPU the apply is fused into the
+    update kernels: the Newton-Schulz final epilogue and the AdamW kernel
+    write ``p + u`` (rounded to the parameter dtype; bfloat16 stochastically
+    when ``stochastic``, with the same noise streams ``apply_updates`` uses
+    for ``key``) instead of the float32 update, which is never written to
+    memory.  ``inplace``: write the new values into the parameter buffers
+    (contiguous leaves in the reference's (batch, R, O) layout), as JAX would
+    with donated parameters.  Other transforms (and the sharded multi-GPU
+    update) run the two calls.  Returns ``(new_params, new_state)``."""
+    if stochastic and key is None:
+        raise ValueError(
+            "apply_updates requires a PRNG `key` when stochastic=True. "
+            "Pass stochastic=False for deterministic rounding."
+        )
+    if getattr(tx.update, "supports_fused_apply", False):
+        return tx.update(grads, state, params, apply_updates=(key, stochastic, inplace))
+    updates, state = tx.update(grads, state, params)
+    return apply_updates(params, updates, key, stochastic), state

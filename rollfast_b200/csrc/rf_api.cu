@@ -104,6 +104,8 @@ struct LeafPlan {
   uint64_t sr_seed;
   float* magma_score;   // Magma score (device), null when off
   int magma_keep;
+  int apply_mode;       // fused parameter apply (0 off, 1 nearest, 2 stochastic bf16)
+  uint64_t apply_seed;
   int64_t magma_chunk;  // first Magma partial-sum chunk of this leaf
 };
 
@@ -209,6 +211,9 @@ static rf_status validate_leaf(const rf_muon_leaf& l, int i, bool need_out) {
     return fail(RF_EINVAL, where + "param (valid dtype) required when decay != 0");
   if (l.mu_dtype != RF_F32 && l.mu_dtype != RF_BF16)
     return fail(RF_EINVAL, where + "mu_dtype must be float32 or bfloat16");
+  if (l.apply_mode < 0 || l.apply_mode > 2) return fail(RF_EINVAL, where + "apply_mode must be 0, 1 or 2");
+  if (l.apply_mode && (!l.param || l.out_dtype != l.param_dtype))
+    return fail(RF_EINVAL, where + "a fused apply needs param, and out in the parameter dtype");
   return RF_OK;
 }
 
@@ -420,6 +425,8 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         f.decay = lp.decay;
         f.decay_dt = lp.decay_dt;
         f.scale_dev = lp.magma_score ? reinterpret_cast<const float*>(base + P.off_factor) + li : nullptr;
+        f.apply_mode = lp.apply_mode;
+        f.apply_seed = lp.apply_seed;
         // Runs of 32 along the leaf's rows: length n (NS columns) for a
         // plain leaf, m (NS rows) for a transposed one.
         f.vec_ok = ((lp.transposed ? gp.m : gp.n) % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.out) % 16 == 0) &&
@@ -540,6 +547,8 @@ static rf_status leaves_from_abi(const rf_muon_leaf* leaves, int32_t n, std::vec
     p.sr_seed = l.sr_seed;
     p.magma_score = l.magma_score;
     p.magma_keep = l.magma_keep ? 1 : 0;
+    p.apply_mode = l.apply_mode;
+    p.apply_seed = l.apply_seed;
     out.push_back(p);
   }
   return RF_OK;
@@ -676,6 +685,9 @@ rf_status rf_muon_update(const rf_muon_leaf* leaves, int32_t n_leaves, const rf_
   RF_TRY(build_plan(lp, p.precision, P, p.aux_stream ? 2 : 1));
   if (p.preconditioning < RF_PRECOND_FROBENIUS || p.preconditioning > RF_PRECOND_SCHATTEN)
     return fail(RF_EINVAL, "unknown preconditioning");
+  for (const LeafPlan& l : P.leaves)
+    if (l.apply_mode && (!p.fuse_tail || p.adaptive))
+      return fail(RF_ENOTSUP, "a fused apply needs fuse_tail = 1 and adaptive = 0");
   if (P.magma_chunks) {
     if (!(p.magma_tau > 0.f)) return fail(RF_EINVAL, "magma_tau must be positive");
     if (p.adaptive) return fail(RF_ENOTSUP, "Magma together with adaptive is not supported");
@@ -983,6 +995,11 @@ rf_status rf_adamw_update(const rf_adam_leaf* leaves, int32_t n_leaves, const rf
       d.seed_mu = l.sr_seed_mu;
       d.seed_nu = l.sr_seed_nu;
       d.mask = l.decay != 0.f ? l.decay_mask : nullptr;
+      if (l.apply_mode < 0 || l.apply_mode > 2) return fail(RF_EINVAL, "adam leaf: apply_mode must be 0, 1 or 2");
+      if (l.apply_mode && (!l.param || l.out_dtype != l.param_dtype))
+        return fail(RF_EINVAL, "adam leaf: a fused apply needs param, and out in the parameter dtype");
+      d.apply_mode = l.apply_mode;
+      d.apply_seed = l.apply_seed;
       d.scale_dev = l.magma_score ? factors + i : nullptr;
       d.vec_ok = (l.n % 8 == 0) && (reinterpret_cast<uintptr_t>(l.grad) % 16 == 0) &&
                  (reinterpret_cast<uintptr_t>(l.mu) % 16 == 0) && (reinterpret_cast<uintptr_t>(l.nu) % 16 == 0) &&

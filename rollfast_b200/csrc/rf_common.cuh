@@ -69,6 +69,38 @@ __device__ __forceinline__ float decay_term(int rdt, float decay, float p) {
   return round_to(rdt, decay * p);
 }
 
+// Stochastic rounding to bfloat16 (utils.py:342-371): 16 bits of noise added
+// below the bf16 significand, then truncation; +-Inf / NaN get no noise.  The
+// noise is the SplitMix64 sequence (Steele, Lea and Flood, "Fast splittable
+// pseudorandom number generators", 2014) of a per-leaf seed: output c serves
+// elements 4c..4c+3, 16 bits each from the low end.
+__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t c) {
+  uint64_t z = seed + (c + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float sr_bf16(float x, uint32_t noise16) {
+  uint32_t b = __float_as_uint(x);
+  if ((b & 0x7FFFFFFFu) >= 0x7F800000u) noise16 = 0u;
+  return __uint_as_float((b + noise16) & 0xFFFF0000u);
+}
+
+__device__ __forceinline__ uint32_t sr_noise(uint64_t seed, int64_t i) {
+  return uint32_t((splitmix64_at(seed, uint64_t(i) >> 2) >> (16 * (i & 3))) & 0xFFFFu);
+}
+
+// A float32 value stored to `dt` at p[i]: bfloat16 with stochastic rounding
+// when `sr` (noise of element i of the seed's stream), else nearest-even.
+__device__ __forceinline__ void st_rounded(void* p, int dt, int64_t i, float v, bool sr, uint64_t seed) {
+  if (sr && dt == RF_BF16) {
+    static_cast<uint16_t*>(p)[i] = uint16_t(__float_as_uint(sr_bf16(v, sr_noise(seed, i))) >> 16);
+  } else {
+    st_from_float(p, dt, i, v);
+  }
+}
+
 inline size_t dtype_size(int dt) { return dt == RF_F32 ? 4 : 2; }
 inline bool valid_dtype(int dt) { return dt == RF_F32 || dt == RF_BF16 || dt == RF_F16; }
 

@@ -130,23 +130,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // bfloat16 optimizer state (utils.py:412-425, adam.py:219-222) and
 // apply_updates.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t c) {
-  uint64_t z = seed + (c + 1) * 0x9E3779B97F4A7C15ull;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ float sr_bf16(float x, uint32_t noise16) {
-  uint32_t b = __float_as_uint(x);
-  if ((b & 0x7FFFFFFFu) >= 0x7F800000u) noise16 = 0u;
-  return __uint_as_float((b + noise16) & 0xFFFF0000u);
-}
-
-__device__ __forceinline__ uint32_t sr_noise(uint64_t seed, int64_t i) {
-  return uint32_t((splitmix64_at(seed, uint64_t(i) >> 2) >> (16 * (i & 3))) & 0xFFFFu);
-}
-
 // v[0..7] -> bf16 at p[i..i+7] (i % 8 == 0, 16-byte aligned), stochastically rounded.
 __device__ __forceinline__ void sr_store8_bf16(void* p, int64_t i, const float* v, uint64_t seed) {
   const uint64_t r0 = splitmix64_at(seed, uint64_t(i) >> 2), r1 = splitmix64_at(seed, (uint64_t(i) >> 2) + 1);
@@ -459,7 +442,7 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
         ld8(L.g, L.gdt, i, g);
         ld8(L.mu, L.sdt, i, mu);
         ld8(L.nu, L.sdt, i, nu);
-        if (L.decay != 0.f) ld8(L.p, L.pdt, i, p);
+        if (L.decay != 0.f || L.apply_mode) ld8(L.p, L.pdt, i, p);
         uint2 mk = make_uint2(0x01010101u, 0x01010101u);
         if (L.mask) mk = *reinterpret_cast<const uint2*>(L.mask + i);
         const uint8_t* mb = reinterpret_cast<const uint8_t*>(&mk);
@@ -473,13 +456,21 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
           st8(L.mu, RF_F32, i, mu);
           st8(L.nu, RF_F32, i, nu);
         }
+        if (L.apply_mode) {  // the new parameter p + u (utils.py:648-708)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) u[k] = __fadd_rn(p[k], u[k]);
+          if (L.apply_mode == 2 && L.odt == RF_BF16) {
+            sr_store8_bf16(L.out, i, u, L.apply_seed);
+            continue;
+          }
+        }
         st8(L.out, L.odt, i, u);
       }
     } else {
       for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float g = ld_as_float(L.g, L.gdt, i);
         float mu = ld_as_float(L.mu, L.sdt, i), nu = ld_as_float(L.nu, L.sdt, i);
-        const float p = L.decay != 0.f ? ld_as_float(L.p, L.pdt, i) : 0.f;
+        const float p = (L.decay != 0.f || L.apply_mode) ? ld_as_float(L.p, L.pdt, i) : 0.f;
         const float u = adam_one(c, L, g, mu, nu, p, L.decay != 0.f && (!L.mask || L.mask[i] != 0));
         if (L.sdt == RF_BF16) {
           sr_store1_bf16(L.mu, i, mu, L.seed_mu);
@@ -488,7 +479,8 @@ __global__ void __launch_bounds__(kEwThreads) k_adamw(const __grid_constant__ Ad
           static_cast<float*>(L.mu)[i] = mu;
           static_cast<float*>(L.nu)[i] = nu;
         }
-        st_from_float(L.out, L.odt, i, u);
+        if (L.apply_mode) st_rounded(L.out, L.odt, i, __fadd_rn(p, u), L.apply_mode == 2, L.apply_seed);
+        else st_from_float(L.out, L.odt, i, u);
       }
     }
   }

@@ -98,6 +98,8 @@ struct AdamLeafDev {
   uint64_t seed_mu, seed_nu;
   const uint8_t* mask;     // optional element-wise decay mask
   const float* scale_dev;  // optional device factor applied after the decay (Magma: keep * score)
+  int32_t apply_mode;      // as in FinalLeaf: write p + u (the new parameter) instead of u
+  uint64_t apply_seed;
 };
 struct AdamLaunch {
   AdamLeafDev leaf[kMaxLeavesPerLaunch];
@@ -163,6 +165,11 @@ struct FinalLeaf {
   float shape_scale, decay;
   int32_t decay_dt;  // dtype decay * p is rounded to (the parameter dtype, or RF_F32)
   const float* scale_dev;  // optional device factor applied after the decay (Magma: keep * score)
+  // Fused parameter apply (utils.py:648-708): 0 off (out = the update);
+  // 1: out = p + u rounded to the parameter dtype (nearest even); 2: the same
+  // with bfloat16 stochastic rounding, noise of element i of apply_seed.
+  int32_t apply_mode;
+  uint64_t apply_seed;
 };
 
 struct NsGemmArgs {
@@ -313,10 +320,15 @@ __device__ __forceinline__ void final_store(const NsGemmArgs& a, const FinalLeaf
   const int64_t idx = bi * a.m * a.n + (L.transposed ? c * a.m + r : r * a.n + c);
   float v = o;
   if (a.fuse_tail) {
+    const float pv = (L.decay != 0.f || L.apply_mode) ? ld_as_float(L.p, L.p_dtype, idx) : 0.f;
     v = __fmul_rn(o, L.shape_scale);
-    if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.decay_dt, L.decay, ld_as_float(L.p, L.p_dtype, idx)));
+    if (L.decay != 0.f) v = __fadd_rn(v, decay_term(L.decay_dt, L.decay, pv));
     if (L.scale_dev) v = __fmul_rn(*L.scale_dev, v);
     v = __fmul_rn(a.neg_lr, v);
+    if (L.apply_mode) {  // the new parameter: p + u in float32, then the parameter dtype
+      st_rounded(L.out, L.out_dtype, idx, __fadd_rn(pv, v), L.apply_mode == 2, L.apply_seed);
+      return;
+    }
   }
   st_from_float(L.out, L.out_dtype, idx, v);
 }
@@ -332,7 +344,7 @@ __device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const Fin
   for (int k = 0; k < 32; ++k) v[k] = o[k];
   if (a.fuse_tail) {
     float pv[32];
-    if (L.decay != 0.f) {
+    if (L.decay != 0.f || L.apply_mode) {
       if (L.p_dtype == RF_F32) {
         const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(L.p) + idx);
 #pragma unroll
@@ -367,6 +379,29 @@ __device__ __forceinline__ void final_store_run32(const NsGemmArgs& a, const Fin
       if (L.decay != 0.f) u = __fadd_rn(u, decay_term(L.decay_dt, L.decay, pv[k]));
       if (L.scale_dev) u = __fmul_rn(fac, u);
       v[k] = __fmul_rn(a.neg_lr, u);
+    }
+    if (L.apply_mode) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = __fadd_rn(pv[k], v[k]);
+      if (L.apply_mode == 2 && L.out_dtype == RF_BF16) {  // stochastic rounding, element idx + k's noise
+        uint4* q = reinterpret_cast<uint4*>(static_cast<uint16_t*>(L.out) + idx);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t r0 = splitmix64_at(L.apply_seed, uint64_t(idx + 8 * j) >> 2);
+          const uint64_t r1 = splitmix64_at(L.apply_seed, (uint64_t(idx + 8 * j) >> 2) + 1);
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const uint64_t r = h < 2 ? r0 : r1;
+            const uint32_t lo = __float_as_uint(sr_bf16(v[8 * j + 2 * h], uint32_t((r >> (32 * (h & 1))) & 0xFFFFu)));
+            const uint32_t hi =
+                __float_as_uint(sr_bf16(v[8 * j + 2 * h + 1], uint32_t((r >> (32 * (h & 1) + 16)) & 0xFFFFu)));
+            w[h] = (lo >> 16) | (hi & 0xFFFF0000u);
+          }
+          q[j] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        return;
+      }
     }
   }
   if (L.out_dtype == RF_F32) {

@@ -48,6 +48,7 @@ from .base import (
     host_count,
     init_empty_state,
     init_magma_state,
+    key_seed,
     magma_keeps,
     new_count,
     partition,
@@ -65,7 +66,9 @@ from .base import (
     validate_beta,
     validate_magma_args,
     validate_positive,
+    _splitmix64,
 )
+from .base import apply_updates as apply_updates_fn
 from .dimension_numbers import (
     MatrixDimensionNumbers,
     MuonDimensionNumbers,
@@ -184,21 +187,23 @@ def _gather_muon_leaves(leaves, mus, ps, specs, transform_name: str, allow_meta:
     return out
 
 
-def _leaf_table(ml: list, scales, decays, decay_f32=None, magma=None):
+def _leaf_table(ml: list, scales, decays, decay_f32=None, magma=None, apply=None):
     """``magma``: None, or (scores, keeps) per leaf (device score tensors and
-    this step's Bernoulli draws)."""
+    this step's Bernoulli draws); ``apply``: None, or (mode, seed) per leaf for
+    the fused parameter apply (``out`` then holds the new parameter)."""
     arr = (_lib.RfMuonLeaf * max(1, len(ml)))()
     for i, L in enumerate(ml):
         b, r, c = L.layout.flat_shape
         e = arr[i]
         e.grad = L.g.data_ptr()
         e.mu = L.mu.data_ptr()
-        e.param = L.p.data_ptr() if (L.p is not None and decays[i] != 0.0) else None
+        needs_p = decays[i] != 0.0 or (apply is not None and apply[i][0])
+        e.param = L.p.data_ptr() if (L.p is not None and needs_p) else None
         e.out = L.out.data_ptr()
         e.batch, e.rows, e.cols = b, r, c
         e.grad_dtype = rf_dtype(L.g)
         e.param_dtype = rf_dtype(L.p) if L.p is not None else _lib.RF_F32
-        e.out_dtype = _lib.RF_F32
+        e.out_dtype = rf_dtype(L.out)
         e.shape_scale = scales[i]
         e.decay = decays[i]
         e.skip_ns = 0
@@ -208,6 +213,8 @@ def _leaf_table(ml: list, scales, decays, decay_f32=None, magma=None):
         if magma is not None:
             e.magma_score = magma[0][i].data_ptr()
             e.magma_keep = int(magma[1][i])
+        if apply is not None:
+            e.apply_mode, e.apply_seed = int(apply[i][0]), int(apply[i][1])
     return arr
 
 
@@ -257,10 +264,10 @@ def run_muon_table(arr, n: int, prm, dev: torch.device) -> None:
     _lib.check(lib.rf_muon_update(arr, n, ctypes.byref(prm), ws.data_ptr(), ws.numel(), main.cuda_stream))
 
 
-def _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32=None, magma=None):
+def _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32=None, magma=None, apply=None):
     if not ml:
         return
-    run_muon_table(_leaf_table(ml, scales, decays, decay_f32, magma), len(ml), prm, ml[0].g.device)
+    run_muon_table(_leaf_table(ml, scales, decays, decay_f32, magma, apply), len(ml), prm, ml[0].g.device)
     del cbuf
 
 
@@ -486,7 +493,9 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
     muon_wd_on = has_nonzero_or_scheduled(weight_decay)
     adam_wd_on = has_nonzero_or_scheduled(eff_adam_wd)
 
-    def fused_update(updates, state, params=None):
+    def fused_update(updates, state, params=None, *, apply_updates=None):
+        """``apply_updates=(key, stochastic, inplace)`` (see ``update_and_apply``):
+        return the new parameters instead of the updates."""
         from . import distributed  # late import: optional torch.distributed plumbing
 
         if params is None:
@@ -593,6 +602,25 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
                                  ns_steps=ns_steps, lr=lr, fuse_tail=1,
                                  reserve_sms=ctx.reserve_sms if sharded else 0,
                                  preconditioning=preconditioning, adaptive=adaptive, magma_tau=magma_tau)
+        fused_apply = apply_updates is not None and not sharded
+        m_apply = a_apply = None
+        if fused_apply:
+            # The final epilogues write p + u straight into the new parameters
+            # (utils.py:648-708): the float32 updates never reach memory.  The
+            # noise seeds are apply_updates' (one stream per leaf position).
+            akey, stoch, inplace = apply_updates
+            seed0 = key_seed(akey) if stoch else 0
+
+            def mode_seed(pos, p):
+                return (2 if (stoch and p.dtype == torch.bfloat16) else 1), (_splitmix64(seed0 + pos) if stoch else 0)
+
+            for L in ml:
+                if L.p is None:
+                    raise ValueError(f"leaf {L.pos}: apply_updates needs its parameter")
+            m_apply = [mode_seed(L.pos, L.p) for L in ml]
+            ml = [L._replace(out=L.p if (inplace and L.layout.is_identity) else
+                             torch.empty(L.layout.flat_shape, dtype=L.p.dtype, device=L.g.device)) for L in ml]
+            a_apply = [mode_seed(pos, ps[pos]) for pos in a_pos]
         res = None
         if owned_only:
             res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds)
@@ -607,9 +635,15 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             if sharded:
                 outs = distributed.sharded_muon_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32)
             else:
-                _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32, mmagma)
+                _run_muon_update(ml, prm, cbuf, scales, decays, decay_f32, mmagma, m_apply)
                 outs = _finish_leaves(ml)
-            a_outs = [torch.empty(it[0].shape, dtype=torch.float32, device=it[0].device) for it in a_items]
+            if fused_apply:
+                a_outs = [ps[pos] if (apply_updates[2] and ps[pos].is_contiguous()) else
+                          torch.empty(ps[pos].shape, dtype=ps[pos].dtype, device=ps[pos].device) for pos in a_pos]
+                a_items = [(it[0], it[1], it[2], ps[pos].contiguous(), *it[4:]) for it, pos in zip(a_items, a_pos)]
+                adam_kw["apply"] = a_apply
+            else:
+                a_outs = [torch.empty(it[0].shape, dtype=torch.float32, device=it[0].device) for it in a_items]
             a_items = [(*it[:4], o, *it[5:]) for it, o in zip(a_items, a_outs)]
             if a_items:
                 # The fallback leaves are independent of the Muon branch: with
@@ -629,7 +663,20 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
                             if t is not None:
                                 t.record_stream(side)
 
-        full = list(leaves)
+        if apply_updates is not None and not fused_apply:
+            # Sharded paths: the updates, then apply_updates as its own pass.
+            full_u = list(leaves)
+            for L, o in zip(ml, outs):
+                full_u[L.pos] = o
+            for i2, o in zip(a_pos, a_outs):
+                full_u[i2] = o
+            outs = [None] * len(ml)
+            applied = apply_updates_fn(tree_unflatten(treedef, ps), tree_unflatten(treedef, full_u), apply_updates[0],
+                                       stochastic=apply_updates[1])
+            ps_new = tree_flatten(applied, is_leaf=is_aux_leaf)[0]
+            outs = [ps_new[L.pos] for L in ml]
+            a_outs = [ps_new[i2] for i2 in a_pos]
+        full = list(ps) if apply_updates is not None else list(leaves)
         for L, o in zip(ml, outs):
             full[L.pos] = o
         for i, o in zip(a_pos, a_outs):
@@ -648,6 +695,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
         })
         return tree_unflatten(treedef, full), new_state
 
+    fused_update.supports_fused_apply = True
     return GradientTransformation(composite.init, fused_update)
 
 
