@@ -622,8 +622,8 @@ def main():
     workload = args.workload if full_size else f"{args.workload}_reduced_{n_layers}_layers_vocab_{args.vocab}"
     model = {"llama3_8b_muon_step": "Llama-3-8B", "llama3_70b_muon_step": "Llama-3-70B",
              "gpt2_small_muon_step": "GPT-2 small"}[args.workload] + f" ({n_layers} layers) parameter set"
-    transport = {"ce+owner_tail": ", copy-engine push of owners' float32 updates into IPC-mapped peer arenas "
-                                  "(AdamW split by element range)",
+    transport = {"ce+owner_tail": ", copy-engine pushes into IPC-mapped peer update arenas: 16-bit O per Muon "
+                                  "bucket (tail on every rank), float32 AdamW updates (split by element range)",
                  "ce": ", copy-engine all-gather of 16-bit O into IPC-mapped peer buffers",
                  "nccl": ", NCCL all-gather"}.get(rf.distributed.active_transport(), "") if world > 1 else ""
     if owned_mode and world > 1:

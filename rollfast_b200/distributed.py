@@ -50,7 +50,8 @@ class ShardContext:
     owned_state: list = field(default_factory=list)  # [(momentum tensor, owner rank)] of the last update
     errors: "ErrorWatch" = None
     steps: int = 0                    # sharded updates run with this context
-    owner_tail: bool = True           # copy-engine transport: owners push final float32 updates
+    owner_tail: bool = True           # copy-engine transport: update arena (AdamW split, pushed float32)
+    fp32_buckets: int = 0             # leading Muon buckets whose owners push float32 updates (rest: O)
     updates: str = "all"              # "all": every rank returns the whole tree; "owned": owners only
 
     def close(self) -> None:
@@ -115,7 +116,8 @@ TRANSPORTS = ("auto", "ce", "nccl")
 
 
 def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None = None,
-              transport: str | None = None, owner_tail: bool | None = None, updates: str = "all") -> ShardContext:
+              transport: str | None = None, owner_tail: bool | None = None, updates: str = "all",
+              fp32_buckets: int | None = None) -> ShardContext:
     """Enable sharded Muon updates over ``group`` (default: the world group).
 
     ``transport``: how owners' leaves reach the other ranks: ``"ce"`` (copy
@@ -124,14 +126,17 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
     ``ce`` when every rank can map its peers' memory, else ``nccl``.
 
     ``owner_tail`` (copy-engine transport; default on, ``ROLLFAST_DIST_OWNER_TAIL=0``
-    turns it off): each owner computes the final float32 updates of its Muon
-    leaves in the fused epilogue, and the AdamW leaves are split by element
-    range, so no rank runs a tail or AdamW over data it does not own; the
-    copy engines push the updates into every peer's update arena, and the
-    returned update tensors are views of that arena, valid until the next
-    update is queued on the caller's stream (``peer.PeerUpdates``).  Off: the
-    owners exchange 16-bit O and every rank runs the tail over all leaves
-    into fresh buffers.
+    turns it off): every rank holds the update tree in one float32 arena that
+    its peers write into (``peer.PeerUpdates``); the returned update tensors
+    are views of it, valid until the next update is queued on the caller's
+    stream.  The AdamW leaves are split by element range: each rank runs
+    AdamW on its range and the copy engines push the float32 updates.  Muon
+    buckets are exchanged as 16-bit O (owners' NS writes O, the copy engines
+    push it, every rank runs the tail into its arena), except the first
+    ``fp32_buckets`` (``ROLLFAST_DIST_FP32_BUCKETS``, default 0), whose owners
+    write the final float32 updates in the fused epilogue and push those:
+    twice the NVLink bytes, no tail.  Off: the gathered-O exchange with
+    AdamW replicated on every rank, into fresh buffers.
 
     ``updates="owned"``: no exchange at all; each rank updates and returns
     only the leaves it owns (``ownership``), for models whose replicated
@@ -152,6 +157,8 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
         transport = os.environ.get("ROLLFAST_DIST_GATHER", "auto") or "auto"
     if owner_tail is None:
         owner_tail = os.environ.get("ROLLFAST_DIST_OWNER_TAIL", "1") != "0"
+    if fp32_buckets is None:
+        fp32_buckets = int(os.environ.get("ROLLFAST_DIST_FP32_BUCKETS", "0") or 0)
     transport = transport.lower()
     if transport not in TRANSPORTS:
         raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
@@ -166,7 +173,7 @@ def configure(group=None, *, buckets: int | None = None, reserve_sms: int | None
         _ctx.close()
     _ctx = ShardContext(rank=dist.get_rank(group), world_size=dist.get_world_size(group), group=group,
                         buckets=max(1, int(buckets)), reserve_sms=max(0, int(reserve_sms)), transport=transport,
-                        owner_tail=bool(owner_tail), updates=updates)
+                        owner_tail=bool(owner_tail), updates=updates, fp32_buckets=max(0, int(fp32_buckets)))
     return _ctx
 
 
@@ -486,6 +493,7 @@ class ArenaPlan:
     adam_offsets: list                # arena offset of each AdamW leaf
     adam_spans: list                  # [(start, end)] of the AdamW region per owner rank
     adam_region: int                  # region index of the AdamW leaves
+    o_regions: set = field(default_factory=set)  # Muon buckets exchanged as 16-bit O
 
 
 def _arena_plan(ctx: ShardContext, ml, a_items, prm, dev):
@@ -498,6 +506,10 @@ def _arena_plan(ctx: ShardContext, ml, a_items, prm, dev):
     regions = [[(i, plan.owner[i], sizes[i]) for i in b.leaves] for b in plan.buckets]
     offs, ranges, total = arena_layout(regions, ctx.world_size)
     muon_offsets = [offs[i] for i in range(len(ml))]
+    o_regions = {b.index for b in plan.buckets if b.index >= ctx.fp32_buckets}
+    o_span = None
+    if o_regions:
+        o_span = (min(ranges[k][0][0] for k in o_regions), max(ranges[k][-1][1] for k in o_regions))
     # AdamW leaves: laid out one after another and split by element count.
     adam_offsets, acc = [], total
     for it in a_items:
@@ -507,31 +519,37 @@ def _arena_plan(ctx: ShardContext, ml, a_items, prm, dev):
     adam_spans = split_range(total, acc - total, ctx.world_size)
     if a_items:
         ranges.append(adam_spans)
-    updates = PeerUpdates.create(ranges, max(acc, 1), ctx, dev, required=ctx.transport == "ce")
+    updates = PeerUpdates.create(ranges, max(acc, 1), ctx, dev, required=ctx.transport == "ce", o_span=o_span,
+                                 o_dtype=_O_DTYPE[prm.precision])
     if updates is None:
         return None
-    return ArenaPlan(plan, updates, muon_offsets, adam_offsets, adam_spans, adam_region)
+    return ArenaPlan(plan, updates, muon_offsets, adam_offsets, adam_spans, adam_region, o_regions)
 
 
 def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, decay_f32, a_items, adam_kw,
                    a_seeds=None):
-    """Sharded Muon branch + AdamW leaves with the owner-side tail (copy-engine
+    """Sharded Muon branch + AdamW leaves over the update arena (copy-engine
     transport).  Returns ``(muon_outs, adam_outs)`` in the order of ``ml`` and
     ``a_items``, or None when the peers cannot be mapped (the caller then
     takes the gathered-O path).
 
     Per step: every rank signals that its stream reached the step; it runs
-    AdamW on its element range of the AdamW leaves and momentum + Newton-Schulz
-    with the fused tail on the Muon leaves it owns, bucket by bucket, each
-    writing final float32 updates into its arena; after each piece the copy
-    engines push the owner's span to every peer; the step ends when every
-    owner's pushes have landed."""
+    AdamW on its element range of the AdamW leaves (final float32 updates in
+    its arena) and momentum + Newton-Schulz on the Muon leaves it owns,
+    bucket by bucket, writing 16-bit O (or, for the first ``fp32_buckets``,
+    final float32 updates through the fused tail); after each piece the copy
+    engines push the owner's span to every peer.  Every rank then runs the
+    tail of the O buckets into its arena, each behind its bucket's arrival,
+    and the step ends when every owner's pushes have landed.  The NVLink
+    bytes per Muon element are 2 for O buckets, 4 for float32 ones: on 8
+    B200s the float32 form slowed the power-capped GEMMs more than the tail it
+    saves (96.5 vs 88.2 ms per Llama-3-8B step), hence O by default."""
     from .adam import run_adam
-    from .base import rf_dtype
+    from .base import rf_dtype, run_tail
     from .muon import _finish_leaves, _leaf_table, run_muon_table
 
     dev = (ml[0].g if ml else a_items[0][0]).device
-    key = ("arena", tuple((L.layout.flat_shape, L.g.dtype) for L in ml),
+    key = ("arena", ctx.fp32_buckets, tuple((L.layout.flat_shape, L.g.dtype) for L in ml),
            tuple((tuple(it[0].shape), it[0].dtype) for it in a_items), prm.n_coeff_rows or prm.ns_steps, dev)
     entry = ctx.plans.get(key)
     if entry is None:
@@ -571,18 +589,37 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
         ev = torch.cuda.Event()
         ev.record(compute)
         up.push(entry.adam_region, ev)
+    fuse = prm.fuse_tail
     for b in plan.buckets:
+        o_mode = b.index in entry.o_regions
         ids = [i for i in b.leaves if plan.owner[i] == ctx.rank]
         if ids:
             sub = [ml[i] for i in ids]
+            if o_mode:  # O (16-bit, leaf layout) into the exchanged buffer; the tail comes after the exchange
+                sub = [L._replace(out=up.o_view(o, L.out.numel()))
+                       for L, o in zip(sub, (entry.muon_offsets[i] for i in ids))]
             arr = _leaf_table(sub, [scales[i] for i in ids], [decays[i] for i in ids],
                               [decay_f32[i] for i in ids])
             for j in range(len(ids)):
                 arr[j].out_dtype = rf_dtype(sub[j].out)
+            prm.fuse_tail = 0 if o_mode else fuse
             run_muon_table(arr, len(ids), prm, dev)
+            prm.fuse_tail = fuse
         ev = torch.cuda.Event()
         ev.record(compute)
-        up.push(b.index, ev)
+        up.push(b.index, ev, o_region=o_mode)
+    # Tails of the O buckets (every rank, the owners' own leaves too, so all
+    # replicas hold identical updates), each behind its bucket's arrival.
+    for b in plan.buckets:
+        if b.index not in entry.o_regions:
+            continue
+        up.wait_region(b.index, compute)
+        items = []
+        for i in b.leaves:
+            L, o = ml[i], entry.muon_offsets[i]
+            p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
+            items.append((up.o_view(o, L.out.numel()), p, L.out.view(-1), scales[i], decays[i], decay_f32[i]))
+        run_tail(items, lr)
     up.finish(compute)
     ctx.owned_state = owned
     ctx.errors.snapshot(compute, ctx.steps)

@@ -301,12 +301,13 @@ class PeerUpdates:
     """The float32 update arena of one ownership plan, mapped by every peer.
 
     Each rank holds the whole sharded update tree in one flat float32 buffer
-    (``arena_layout``).  An owner's fused Newton-Schulz epilogue (and its
-    AdamW slice) writes the final updates ``-lr (shape O + decay p)`` of its
-    leaves straight into its own arena; the copy engines then push each
-    owner's span of a region into the same span of every peer's arena.  No
-    rank runs a tail over leaves it does not own, and the update tensors the
-    step returns are views of the arena.
+    (``arena_layout``); the update tensors the step returns are views of it.
+    A region (a Muon bucket, or the AdamW leaves) reaches the peers in one of
+    two forms: the owners' final float32 updates, written into the owner's
+    arena by the fused epilogue or the AdamW kernel and pushed span by span;
+    or the owners' 16-bit O, written into a 16-bit buffer mirroring the
+    arena's offsets (``o_buf``) and pushed, after which every rank runs the
+    tail ``-lr (shape O + decay p)`` into its arena.
 
     Ordering, with epoch ``e`` per step and flags ``arrive[region][sender]``
     then ``ready[sender]``:
@@ -324,11 +325,17 @@ class PeerUpdates:
     Updates returned by step e therefore stay valid until the next update is
     queued on the caller's stream."""
 
-    def __init__(self, ranges, total, rank, world_size, group, device, timeout_s=None):
+    def __init__(self, ranges, total, rank, world_size, group, device, timeout_s=None, o_span=None,
+                 o_dtype=torch.float16):
         self.ranges, self.rank, self.world, self.group = ranges, rank, world_size, group
         self.device = device
         self.timeout_s = default_timeout_s() if timeout_s is None else float(timeout_s)
         self.arena = torch.empty(total, dtype=torch.float32, device=device)
+        # Optional 16-bit O buffer for the regions exchanged as O: it mirrors
+        # the arena's element offsets over [o_base, o_base + len).
+        self.o_base = o_span[0] if o_span else 0
+        self.o_buf = (torch.empty(max(o_span[1] - o_span[0], 1), dtype=o_dtype, device=device) if o_span
+                      else None)
         self.n_regions = len(ranges)
         if self.n_regions * world_size > 64:
             raise ValueError("too many exchange regions for one flag wait (regions x ranks must be <= 64)")
@@ -339,10 +346,11 @@ class PeerUpdates:
         self.copy_stream = torch.cuda.Stream(device=device)
 
     @classmethod
-    def create(cls, ranges, total, ctx, device, *, required: bool):
-        g = cls(ranges, total, ctx.rank, ctx.world_size, ctx.group, device)
+    def create(cls, ranges, total, ctx, device, *, required: bool, o_span=None, o_dtype=torch.float16):
+        g = cls(ranges, total, ctx.rank, ctx.world_size, ctx.group, device, o_span=o_span, o_dtype=o_dtype)
         torch.cuda.synchronize(device)  # flags are zero before any peer can signal
-        remote, mapped, why = _map_peer_buffers(ctx, [g.arena, g.flags], required)
+        bufs = [g.arena, g.flags] + ([g.o_buf] if g.o_buf is not None else [])
+        remote, mapped, why = _map_peer_buffers(ctx, bufs, required)
         if why is not None:
             return None
         g.remote, g._mapped = remote, mapped
@@ -373,18 +381,33 @@ class PeerUpdates:
         readys = self.flags.data_ptr() + 4 * self.n_regions * self.world
         _lib.flags_wait(readys, self.world, self.rank, self.epoch, self.timeout_s, self.copy_stream.cuda_stream)
 
-    def push(self, k: int, ready: torch.cuda.Event) -> None:
-        """Push this rank's span of region ``k`` (complete at ``ready``)."""
+    def o_view(self, start: int, n: int) -> torch.Tensor:
+        """The 16-bit O buffer's elements at arena offsets [start, start + n)."""
+        return self.o_buf[start - self.o_base: start - self.o_base + n]
+
+    def push(self, k: int, ready: torch.cuda.Event, o_region: bool = False) -> None:
+        """Push this rank's span of region ``k`` (complete at ``ready``): the
+        float32 updates, or (``o_region``) the 16-bit O of that span."""
         start, end = self.ranges[k][self.rank]
         s = self.copy_stream
         s.wait_event(ready)
-        nbytes = (end - start) * 4
-        if nbytes:
-            src = self.arena.data_ptr() + start * 4
+        if end > start:
+            if o_region:
+                es = self.o_buf.element_size()
+                off = (start - self.o_base) * es
+                src, nbytes, buf = self.o_buf.data_ptr() + off, (end - start) * es, 2
+            else:
+                off = start * 4
+                src, nbytes, buf = self.arena.data_ptr() + off, (end - start) * 4, 0
             for r in self._peers():
-                _lib.peer_copy(self.remote[r][0] + start * 4, src, nbytes, s.cuda_stream)
+                _lib.peer_copy(self.remote[r][buf] + off, src, nbytes, s.cuda_stream)
         idx = k * self.world + self.rank
         _lib.flags_signal([self._flag_addr(r, idx) for r in range(self.world)], self.epoch, s.cuda_stream)
+
+    def wait_region(self, k: int, stream: torch.cuda.Stream) -> None:
+        """Block ``stream`` until every owner's span of region ``k`` has landed."""
+        _lib.flags_wait(self.flags.data_ptr() + 4 * k * self.world, self.world, -1, self.epoch, self.timeout_s,
+                        stream.cuda_stream)
 
     def finish(self, compute: torch.cuda.Stream) -> None:
         """Order ``compute`` after every owner's pushes of this step."""

@@ -10,6 +10,11 @@ schedule for 5 and 8 iterations.  TFLOP/s counts the dense algorithmic NS
 FLOPs (4 m^2 n + 2 m^3 per matrix per iteration, m <= n) over the CUDA-event
 time of the whole call (normalisation pass included); ``gemm`` is the same
 FLOPs over the GEMM-kernel time alone (per-launch events).
+
+``--graph``: the call is captured once in a CUDA graph and replayed, so small
+shapes are timed without the host's per-launch cost (the 18 launches of a
+5-iteration call take longer to issue than to run below ~2048^2); the
+reported ``tflops`` is then the graph replay's.
 """
 
 from __future__ import annotations
@@ -36,7 +41,7 @@ def peak_tflops() -> tuple[float, str]:
     return 1590.0, "fallback bf16 burst"
 
 
-def run_case(m: int, n: int, batch: int, iters: int, reps: int, warmup: int, dev) -> dict:
+def run_case(m: int, n: int, batch: int, iters: int, reps: int, warmup: int, dev, graph: bool = False) -> dict:
     g = torch.Generator(device=dev)
     g.manual_seed(m * 131 + n)
     x = torch.randn((batch, m, n), device=dev, generator=g)
@@ -45,6 +50,23 @@ def run_case(m: int, n: int, batch: int, iters: int, reps: int, warmup: int, dev
     for _ in range(warmup):
         out = quintic_newton_schulz(x, coeffs, iters)
     torch.cuda.synchronize()
+    graph_ms = None
+    if graph:
+        # The workspace exists after the warm-up, so capture allocates only
+        # the output (from the graph's pool); every launch is recorded.
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            gout = quintic_newton_schulz(x, coeffs, iters)
+        cg.replay()
+        torch.cuda.synchronize()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record()
+        for _ in range(reps):
+            cg.replay()
+        ge.record()
+        torch.cuda.synchronize()
+        graph_ms = gs.elapsed_time(ge) / reps
+        del gout, cg
     _lib.profile_begin()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
@@ -57,7 +79,11 @@ def run_case(m: int, n: int, batch: int, iters: int, reps: int, warmup: int, dev
     mm, nn = min(m, n), max(m, n)
     flops = batch * iters * (4 * mm * mm * nn + 2 * mm ** 3)
     del out
-    return {"m": m, "n": n, "batch": batch, "iters": iters, "ms": round(ms, 3),
+    extra = {}
+    if graph_ms is not None:
+        extra = {"eager_ms": round(ms, 3), "eager_tflops": round(flops / (ms * 1e-3) / 1e12, 1), "graph": True}
+        ms = graph_ms
+    return {"m": m, "n": n, "batch": batch, "iters": iters, "ms": round(ms, 3), **extra,
             "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "gemm_tflops": round(prof["algorithmic_flops"] / (prof["gemm_ms"] * 1e-3) / 1e12, 1)
             if prof["gemm_ms"] else None,
@@ -73,6 +99,7 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--precision", default="f16")
+    ap.add_argument("--graph", action="store_true", help="time CUDA-graph replays of the call")
     args = ap.parse_args(argv)
     _runtime.set_ns_precision(args.precision)
     dev = torch.device("cuda", 0)
@@ -80,7 +107,7 @@ def main(argv=None):
     peak, src = peak_tflops()
     for m, n in shapes:
         for it in (int(v) for v in args.iters.split(",")):
-            r = run_case(m, n, args.batch, it, args.reps, args.warmup, dev)
+            r = run_case(m, n, args.batch, it, args.reps, args.warmup, dev, graph=args.graph)
             r["frac_of_peak"] = round(r["tflops"] / peak, 3)
             r["peak"] = f"{peak} ({src})"
             r["precision"] = args.precision
