@@ -411,22 +411,33 @@ def rel_err(a, b) -> float:
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
+def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist, rf=None):
     """Same step through host buffers: pinned gradients copied H2D and the
-    update tree copied D2H inside the timed region, every step."""
+    update tree copied D2H inside the timed region, every step.  On one GPU
+    the whole tree both ways.  Sharded, the host holds one gradient tree and
+    receives one update tree, split across the GPUs: each rank copies in the
+    gradient elements it owns and copies out the update elements it computed
+    (``distributed.owned_parts``); under updates="owned" that is its owned
+    leaves."""
     torch.cuda.empty_cache()
     dev_g = grad_sets[1]
-    # Leaves this rank holds (under updates="owned" the others are meta).
-    real = [not t.is_meta for t in leaves_of(dev_g)]
-    host_g = [torch.empty(t.shape, dtype=torch.bfloat16, pin_memory=True) if r else None
-              for t, r in zip(leaves_of(grad_sets[0]), real)]
-    for hg, dg in zip(host_g, leaves_of(grad_sets[0])):
-        if hg is not None:
-            hg.copy_(dg)
-    host_u = [torch.empty(t.shape, dtype=torch.float32, pin_memory=True) if r else None
-              for t, r in zip(leaves_of(dev_g), real)]
-    h2d = sum(t.numel() * t.element_size() for t in host_g if t is not None)
-    d2h = sum(t.numel() * t.element_size() for t in host_u if t is not None)
+    flat = leaves_of(dev_g)
+    # (flat leaf view, element range) this rank copies, per leaf.
+    if dist is not None and rf is not None and any(rf.distributed.owned_parts()):
+        muon_pos, adam_parts = rf.distributed.owned_parts()
+        ranges = {p: (0, flat[p].numel()) for p in muon_pos}
+        ranges.update({p: (a, b) for p, a, b in adam_parts})
+    else:
+        ranges = {p: (0, t.numel()) for p, t in enumerate(flat) if not t.is_meta}
+    pos = sorted(ranges)
+    host_g = [torch.empty(ranges[p][1] - ranges[p][0], dtype=torch.bfloat16, pin_memory=True) for p in pos]
+    src0 = leaves_of(grad_sets[0])
+    for hg, p in zip(host_g, pos):
+        a, b = ranges[p]
+        hg.copy_(src0[p].reshape(-1)[a:b])
+    host_u = [torch.empty(ranges[p][1] - ranges[p][0], dtype=torch.float32, pin_memory=True) for p in pos]
+    h2d = sum(t.numel() * t.element_size() for t in host_g)
+    d2h = sum(t.numel() * t.element_size() for t in host_u)
     k = args.e2e_steps or max(2, min(args.steps, 5))
     upd, state = tx.update(dev_g, state, params)  # warm the output allocations
     del upd
@@ -434,13 +445,14 @@ def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(k):
-        for hg, dg in zip(host_g, leaves_of(dev_g)):
-            if hg is not None:
-                dg.copy_(hg, non_blocking=True)
+        for hg, p in zip(host_g, pos):
+            a, b = ranges[p]
+            flat[p].view(-1)[a:b].copy_(hg, non_blocking=True)
         upd, state = tx.update(dev_g, state, params)
-        for hu, du in zip(host_u, leaves_of(upd)):
-            if hu is not None:
-                hu.copy_(du, non_blocking=True)
+        ups = leaves_of(upd)
+        for hu, p in zip(host_u, pos):
+            a, b = ranges[p]
+            hu.copy_(ups[p].reshape(-1)[a:b], non_blocking=True)
         upd = None  # the copies are stream-ordered before any reuse of these blocks
     e1.record()
     barrier()
@@ -449,8 +461,12 @@ def run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist):
         t = torch.tensor([e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
+    split = dist is not None and rf is not None and any(rf.distributed.owned_parts())
     return {"value": round(e_ms, 2), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": k, "path": "rollfast_b200.muon(...).update with pinned host grads/updates"}
+            "steps": k, "bytes": "per rank" if dist is not None else "whole tree",
+            "path": "rollfast_b200.muon(...).update with pinned host grads/updates"
+                    + (": each rank copies the gradient elements it owns in and the updates it computed out"
+                       if split else "")}
 
 
 def main():
@@ -603,7 +619,7 @@ def main():
     e2e = None
     if not args.no_e2e and not args.apply_updates:
         try:
-            e2e = run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist)
+            e2e = run_e2e(args, tx, state, params, grad_sets, shapes, dev, barrier, dist, rf)
         except (RuntimeError, MemoryError) as exc:  # host RAM for pinned buffers
             e2e = {"value": None, "unit": "ms", "unavailable": f"{type(exc).__name__}: {exc}"[:200]}
         grad_sets = None

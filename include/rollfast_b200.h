@@ -176,7 +176,8 @@ rf_status rf_newton_schulz(const void* x, int32_t x_dtype, void* out, int32_t ou
  * call writes every byte it reads), so calls that overlap on the GPU race:
  * keep them on one stream.  The first call on a device looks the array's
  * address up (cudaGetSymbolAddress) and should come before any stream
- * capture.  Never calls cudaMalloc / cudaFree. */
+ * capture; that address belongs to the context current then (after a
+ * cudaDeviceReset, use a new process).  Never calls cudaMalloc / cudaFree. */
 #define RF_NS_NOALLOC_MAX_WORKSPACE ((size_t)32 << 20)
 rf_status rf_newton_schulz_noalloc(const void* x, int32_t x_dtype, void* out, int32_t out_dtype,
                                    int64_t batch, int64_t rows, int64_t cols, const float* coeffs,

@@ -22,7 +22,9 @@
 //     one stream.
 //   * The device address of the array is looked up once per device with
 //     cudaGetSymbolAddress, by the first call made with that device current;
-//     make that first call before any stream capture.
+//     make that first call before any stream capture.  The address belongs to
+//     the CUDA context current at that call: after a cudaDeviceReset, or
+//     from another context on the same device, use a new process.
 // The computation is the one rf_newton_schulz performs (same kernels).
 #include <mutex>
 

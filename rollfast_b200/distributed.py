@@ -52,6 +52,7 @@ class ShardContext:
     steps: int = 0                    # sharded updates run with this context
     owner_tail: bool = True           # copy-engine transport: update arena (AdamW split, pushed float32)
     fp32_buckets: int = 0             # leading Muon buckets whose owners push float32 updates (rest: O)
+    last_parts: tuple = ((), ())      # see owned_parts()
     updates: str = "all"              # "all": every rank returns the whole tree; "owned": owners only
 
     def close(self) -> None:
@@ -527,7 +528,7 @@ def _arena_plan(ctx: ShardContext, ml, a_items, prm, dev):
 
 
 def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, decay_f32, a_items, adam_kw,
-                   a_seeds=None):
+                   a_seeds=None, a_pos=()):
     """Sharded Muon branch + AdamW leaves over the update arena (copy-engine
     transport).  Returns ``(muon_outs, adam_outs)`` in the order of ``ml`` and
     ``a_items``, or None when the peers cannot be mapped (the caller then
@@ -622,6 +623,14 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
         run_tail(items, lr)
     up.finish(compute)
     ctx.owned_state = owned
+    adam_parts = []
+    if a_items:
+        lo, hi = entry.adam_spans[ctx.rank]
+        for pos, it, o in zip(a_pos, a_items, entry.adam_offsets):
+            a, b = max(lo - o, 0), min(hi - o, it[0].numel())
+            if a < b:
+                adam_parts.append((pos, a, b))
+    ctx.last_parts = (tuple(L.pos for i, L in enumerate(ml) if plan.owner[i] == ctx.rank), tuple(adam_parts))
     ctx.errors.snapshot(compute, ctx.steps)
     return _finish_leaves(ml), a_outs
 
@@ -709,7 +718,20 @@ def owned_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, decay_f32, a_
         a_outs.append(o)
     run_adam(items, seeds=seeds if a_seeds is not None else None, **adam_kw)
     ctx.owned_state = []
+    ctx.last_parts = (tuple(L.pos for L, r in zip(ml, mo) if r == ctx.rank), ())
     return outs, a_outs
+
+
+def owned_parts(ctx: ShardContext | None = None) -> tuple:
+    """What this rank computed in the context's last sharded update:
+    ``(muon_positions, adam_ranges)`` -- the tree positions (flattened leaf
+    order) of the Muon leaves it owns, and ``(position, start, end)`` element
+    ranges of the AdamW leaves it owns.  Those are the gradient elements the
+    rank reads and the update elements it produces, so a host pipeline that
+    holds one gradient tree can feed each rank only its part (the update
+    arena then holds every rank's results)."""
+    ctx = ctx or _ctx
+    return ctx.last_parts if ctx is not None else ((), ())
 
 
 def consolidate_momentum(ctx: ShardContext | None = None) -> int:

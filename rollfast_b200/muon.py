@@ -626,7 +626,7 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds)
         elif sharded and ctx.owner_tail and ctx.transport in ("ce", "auto") and not adaptive and (ml or a_items):
             res = distributed.sharded_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32, a_items, adam_kw,
-                                             a_seeds)
+                                             a_seeds, a_pos)
             if res is None:
                 ctx.owner_tail = False  # peers cannot be mapped (same answer on every rank)
         if res is not None:
