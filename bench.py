@@ -9,6 +9,8 @@ tree: 224 Muon matrix leaves (32 layers x q,k,v,o,gate,up,down, bf16) and the
 AdamW fallback leaves (65 RMSNorm vectors, 128256x4096 embed and unembed).
 Gradients are N(0,1) bf16 (two seeded sets, alternated so consecutive steps
 differ); inputs (16 GB) are far larger than L2, so no flush is needed.
+``--workload`` selects the other configurations (GPT-2 small, Llama-3-70B on
+more than one GPU); their lines name their own metric and L2 note.
 
 Printed JSON (rank 0): ``value`` = ms per step (max over ranks, CUDA events),
 ``e2e`` = the same through host buffers (pinned gradients H2D + updates D2H
@@ -644,10 +646,14 @@ def main():
                  "nccl": ", NCCL all-gather"}.get(rf.distributed.active_transport(), "") if world > 1 else ""
     if owned_mode and world > 1:
         transport = ", owners keep their leaves' updates (no exchange: the float32 update tree does not fit a GPU)"
+    grad_gb = sum(math.prod(s) for s in leaves_of(shapes)) * 2 / 1e9  # one bf16 gradient set
+    # The traffic figure comes from a capture of the Llama-3-8B 4096x14336
+    # sub-batch launches; other workloads' launches hold other shapes.
+    traffic = TRAFFIC_PER_LAUNCH if (full_size and args.workload == "llama3_8b_muon_step") else None
 
     if rank == 0:
         out = {
-            "metric": METRIC,
+            "metric": METRIC if args.workload == "llama3_8b_muon_step" else model.split(" (")[0] + " Muon step ms",
             "value": round(ms, 2),
             "unit": "ms",
             "n_gpus": world,
@@ -668,7 +674,8 @@ def main():
                        "adam_leaves": len(leaves_of(shapes)) - len(muon_matrix_shapes(shapes)), "ns_steps": 5,
                        "ns_coeffs": muon_kw.get("ns_coeffs", "standard"),
                        "options": {k: v for k, v in muon_kw.items() if k != "ns_coeffs"},
-                       "l2": "inputs (>= 16 GB grads) >> 126 MB L2; no flush",
+                       "l2": (f"inputs ({grad_gb:.2f} GB bf16 grads per step, plus state) > 126 MB L2; no flush"
+                              if grad_gb > 0.126 else f"reduced: {grad_gb:.3f} GB of grads per step can sit in L2"),
                        "parallelism": f"muon leaves FLOP-balanced over {world} GPU(s)" + transport},
             "ns_tflops_algorithmic": round(ns_alg_flops(shapes) / (ms * 1e-3) / 1e12, 1),
             "roofline": {
@@ -684,7 +691,7 @@ def main():
                 "gemm_ms_per_step": round(prof["gemm_ms"] / args.steps, 2),
                 # DRAM read+write bytes per launch of the 4096x14336 sub-batch
                 # stages (80% of the step's FLOPs): see TRAFFIC_PER_LAUNCH.
-                "traffic": TRAFFIC_PER_LAUNCH if (full_size and not owned_mode) else None,
+                "traffic": traffic,
                 "traffic_unit": "bytes per launch",
             },
             "gpu_launches": launches,
