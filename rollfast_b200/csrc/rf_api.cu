@@ -64,6 +64,16 @@ rf_status snapshot_peer_error(int32_t* dst, cudaStream_t st);    // rf_peer.cu
 // ---------------------------------------------------------------------------
 static float f32_pow(float b, int e) { return float(std::pow(double(b), double(e))); }
 
+// Programmatic dependent launch of the Newton-Schulz stages (on unless
+// ROLLFAST_NS_PDL=0, which launches every stage plainly; results are the same).
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("ROLLFAST_NS_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static MomentumCoeffs momentum_coeffs(const rf_muon_params& p) {
   MomentumCoeffs c{};
   const float beta = p.beta;
@@ -476,12 +486,17 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
       }
 
       // ---- Newton-Schulz GEMM stages on st ----
+      // Every stage but the first directly follows another stage on st and
+      // is launched as its programmatic dependent (its prologue overlaps the
+      // previous stage's drain); the first follows the operand load and, on
+      // the multi-stream path, an event join, and is launched plainly.
       uint8_t* xc = X0;
       uint8_t* xn = X1;
       for (int it = 0; it < ns_steps; ++it) {
         const float* cf = coeffs + 3 * (n_coeff_rows == 0 ? 0 : it);
         const float ca = cf[0], cb = cf[1], cc = cf[2];
         // A~ = (sa / sx^2) X~ X~^T
+        ga.pdl = it > 0 && pdl_enabled();
         ga.stage = kSyrkXXt;
         ga.a_op = ga.b_op = xc;
         ga.aux = nullptr;
@@ -490,6 +505,7 @@ static rf_status run_pipeline(const Plan& P, const MomentumCoeffs& mc, const flo
         ga.beta = 0.f;
         RF_TRY(launch_ns_gemm(ga, st));
         // B~ = sb (b A + c A A) = (c sb / sa^2) A~ A~ + (b sb / sa) A~
+        ga.pdl = pdl_enabled();
         ga.stage = kSyrkPoly;
         ga.a_op = ga.b_op = ga.aux = Am;
         ga.out = Bm;

@@ -176,6 +176,7 @@ struct NsGemmArgs {
   int stage;
   int precision;       // rf_ns_precision (operand storage)
   int reserve_sms;     // SMs the persistent grid leaves free
+  int pdl;             // launch as a programmatic dependent of the previous stage on the stream
   int64_t G;           // matrices in the group
   int64_t m, n;        // true NS dims (m <= n)
   int64_t mp, np;      // padded dims

@@ -99,6 +99,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// Programmatic dependent launch.  A stage launched with the programmatic
+// stream serialization attribute may be scheduled while the previous stage
+// drains; it touches global memory only after griddepcontrol.wait, which
+// returns once the previous grid has completed and its writes are visible
+// (at once for a launch without the attribute).  launch_dependents, issued by
+// every CTA after that wait, lets the next stage's CTAs take the SMs this
+// grid vacates and run their prologue (barrier init, TMEM allocation) there.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
@@ -221,14 +232,32 @@ __device__ __forceinline__ void record_error(int code, volatile int* abort_flag)
   atomicCAS(&g_tc_error, 0, code);
 }
 
+// The epilogue's second operand (A~ for the polynomial stage, X~ for the B X
+// stages) for one 32-column chunk: 32 16-bit values of row row0 + lane.  The
+// epilogue loads chunk c + 1 while it finishes chunk c, and a tile's first
+// chunk before it waits for the accumulator, so these loads overlap the MMA
+// and the previous chunk's stores instead of stalling each chunk.  Lanes
+// whose symmetric chunk lies wholly below the diagonal load nothing.
+template <typename T>
+__device__ __forceinline__ void load_aux_chunk(const NsGemmArgs& a, bool sym, int64_t g, int64_t row0, int64_t col0,
+                                               int lane, uint4 (&x)[4]) {
+  const int64_t ldc = sym ? a.mp : a.np;
+  const int64_t row = row0 + lane;
+  if (sym && col0 + 31 < row) return;
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const T*>(a.aux) + g * a.mp * ldc + row * ldc + col0);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) x[q] = p[q];
+}
+
 // One 32-column chunk of the epilogue.  The calling warp holds rows
 // row0..row0+31 (lane = row - row0) of matrix g, columns col0..col0+31 of the
-// accumulator in v[].  Stages: symmetric (upper-triangle store + mirror),
-// general (fused a X + B X), final (O, or the fused tail, into the leaf).
+// accumulator in v[] and, for the stages with a second operand, that
+// operand's chunk in xin[] (load_aux_chunk).  Stages: symmetric
+// (upper-triangle store + mirror), general (fused a X + B X), final (O, or
+// the fused tail, into the leaf).
 template <typename T>
 __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, int64_t g, int64_t row0, int64_t col0,
-                                               int lane, int fl, const float* v, float* stg) {
-  const T* aux = static_cast<const T*>(a.aux);
+                                               int lane, int fl, const float* v, const uint4 (&xin)[4], float* stg) {
   T* out = static_cast<T*>(a.out);
   const int64_t ldc = sym ? a.mp : a.np;
   const int64_t mat_off = g * a.mp * ldc;
@@ -238,9 +267,8 @@ __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, in
   if (sym) {
     if (col0 + 31 < row) return;  // whole chunk below the diagonal (no warp-collective work follows)
     if (a.stage == kSyrkPoly) {
-      const uint4* ap = reinterpret_cast<const uint4*>(aux + rbase);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) Vec16<T>::unpack(ap[q], f + 8 * q);
+      for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xin[q], f + 8 * q);
 #pragma unroll
       for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
     } else {
@@ -268,9 +296,8 @@ __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, in
     }
     return;
   }
-  const uint4* xp = reinterpret_cast<const uint4*>(aux + rbase);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xp[q], f + 8 * q);
+  for (int q = 0; q < 4; ++q) Vec16<T>::unpack(xin[q], f + 8 * q);
 #pragma unroll
   for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
   if (a.stage == kGemmBX) {
@@ -321,6 +348,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dependency_wait();
+  allow_dependent_launch();
   const uint32_t tmem_base = *tmem_slot;
   const NsGemmArgs& a = P.a;
 
@@ -428,6 +457,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const bool has_aux = a.stage != kSyrkXXt;
     int acc = 0;
     uint32_t acc_phase = 0;
     float* stg = epi_stage + (warp - 2) * (32 * 33);
@@ -435,19 +465,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int64_t g;
       int I, J;
       decode_tile(P, t, g, I, J);
+      const int64_t row0 = int64_t(I) * BM + quarter * 32;
+      const int64_t col_base = int64_t(J) * BN;
+      uint4 xnext[4] = {};
+      if (has_aux) load_aux_chunk<T>(a, P.sym, g, row0, col_base, lane, xnext);
       if (!mbar_wait(accf0 + 8 * acc, acc_phase, abort_flag)) {
         record_error(kDevTimeoutEpilogue, abort_flag);
         break;
       }
       tc_fence_after();
-      const int64_t row0 = int64_t(I) * BM + quarter * 32;
       int fl = 0;
       if (a.stage == kGemmBXFinal) fl = find_final_leaf(a, g);
       for (int ch = 0; ch < BN / 32; ++ch) {
+        const uint4 xcur[4] = {xnext[0], xnext[1], xnext[2], xnext[3]};
+        if (has_aux && ch + 1 < BN / 32) load_aux_chunk<T>(a, P.sym, g, row0, col_base + (ch + 1) * 32, lane, xnext);
         float v[32];
         __syncwarp();  // tcgen05.ld is warp-collective; lanes may have diverged on the diagonal
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + ch * 32), v);
-        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * BN + ch * 32, lane, fl, v, stg);
+        epilogue_chunk<T>(a, P.sym, g, row0, col_base + ch * 32, lane, fl, v, xcur, stg);
       }
       tc_fence_before();
       mbar_arrive(acce0 + 8 * acc);
@@ -621,6 +656,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
+  grid_dependency_wait();
+  allow_dependent_launch();
   const uint32_t tmem_base = *tmem_slot;
   const NsGemmArgs& a = P.a;
 
@@ -733,6 +770,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- Epilogue (warps 2..5 of both CTAs) ----------------
     const int quarter = warp & 3;
+    const bool has_aux = a.stage != kSyrkXXt;
     int acc = 0;
     uint32_t acc_phase = 0;
     float* stg = epi_stage + (warp - 2) * (32 * 33);
@@ -740,19 +778,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int64_t g;
       int I, J;
       decode_tile2(P, t, g, I, J);
+      const int64_t row0 = int64_t(I) * 256 + int64_t(rank) * BM + quarter * 32;
+      const int64_t col_base = int64_t(J) * 256;
+      uint4 xnext[4] = {};
+      if (has_aux) load_aux_chunk<T>(a, P.sym, g, row0, col_base, lane, xnext);
       if (!mbar_wait(accf0 + 8 * acc, acc_phase, abort_flag)) {
         record_error(kDevTimeoutEpilogue, abort_flag);
         break;
       }
       tc_fence_after();
-      const int64_t row0 = int64_t(I) * 256 + int64_t(rank) * BM + quarter * 32;
       int fl = 0;
       if (a.stage == kGemmBXFinal) fl = find_final_leaf(a, g);
       for (int ch = 0; ch < 256 / 32; ++ch) {
+        const uint4 xcur[4] = {xnext[0], xnext[1], xnext[2], xnext[3]};
+        if (has_aux && ch + 1 < 256 / 32) load_aux_chunk<T>(a, P.sym, g, row0, col_base + (ch + 1) * 32, lane, xnext);
         float v[32];
         __syncwarp();
         tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * 256 + ch * 32), v);
-        epilogue_chunk<T>(a, P.sym, g, row0, int64_t(J) * 256 + ch * 32, lane, fl, v, stg);
+        epilogue_chunk<T>(a, P.sym, g, row0, col_base + ch * 32, lane, fl, v, xcur, stg);
       }
       tc_fence_before();
       __syncwarp();
@@ -808,6 +851,28 @@ rf_status make_map(CUtensorMap* map, const void* base, int precision, int64_t G,
   return RF_OK;
 }
 
+// One stage launch of NUM_THREADS-thread CTAs (the pair kernel's cluster
+// shape is compiled in).  With pdl the launch carries the programmatic
+// stream serialization attribute: the kernel may start while the previous
+// kernel on the stream drains and orders itself with griddepcontrol.wait.
+template <typename Kernel, typename Params>
+rf_status launch_stage(Kernel kernel, unsigned grid, int smem, int pdl, cudaStream_t st, const CUtensorMap& mA,
+                       const CUtensorMap& mB, const Params& P) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mA, mB, P);
+  if (e != cudaSuccess) return fail(RF_ECUDA, std::string("NS stage launch: ") + cudaGetErrorString(e));
+  return RF_OK;
+}
+
 template <typename T>
 rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
   static std::once_flag once;
@@ -841,7 +906,7 @@ rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
   int64_t cap = num_sms() - a.reserve_sms;
   if (cap < 1) cap = 1;
   const int64_t grid = P.total_tiles < cap ? P.total_tiles : cap;
-  k_ns_tc<T><<<unsigned(grid), NUM_THREADS, SMEM_BYTES, st>>>(mA, mB, P);
+  RF_TRY(launch_stage(k_ns_tc<T>, unsigned(grid), SMEM_BYTES, a.pdl, st, mA, mB, P));
   return check_launch("k_ns_tc");
 }
 
@@ -889,7 +954,7 @@ rf_status launch_typed(const NsGemmArgs& a, cudaStream_t st) {
   int64_t cap = pairs_max - (a.reserve_sms + 1) / 2;
   if (cap < 1) cap = 1;
   const int64_t pairs = P.total_tiles < cap ? P.total_tiles : cap;
-  k_ns_tc2<T><<<unsigned(2 * pairs), NUM_THREADS, SMEM_BYTES, st>>>(mA, mB, P);
+  RF_TRY(launch_stage(k_ns_tc2<T>, unsigned(2 * pairs), SMEM_BYTES, a.pdl, st, mA, mB, P));
   return check_launch("k_ns_tc2");
 }
 }  // namespace tc2
