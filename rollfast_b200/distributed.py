@@ -568,10 +568,16 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
     ml = [L._replace(out=arena[o: o + L.out.numel()].view(L.out.shape)) for L, o in zip(ml, entry.muon_offsets)]
     a_outs = [arena[o: o + it[0].numel()].view(it[0].shape) for it, o in zip(a_items, entry.adam_offsets)]
     owned = [(L.mu_state, plan.owner[i]) for i, L in enumerate(ml)]
+    trace = _Trace(compute, up.copy_stream) if os.environ.get("ROLLFAST_DIST_PROFILE") == "1" else None
+
+    def mark(stream, label):
+        if trace is not None:
+            trace.mark(stream, label)
 
     up.begin_step(compute)
     # AdamW first: its push overlaps the first bucket's Newton-Schulz.
     if a_items:
+        mark("compute", "adam")
         mine, seeds = [], []
         for j, (it, o, out) in enumerate(zip(a_items, entry.adam_offsets, a_outs)):
             g, mu, nu, p = it[0], it[1], it[2], it[3]
@@ -587,13 +593,16 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
                     if a_seeds is not None:  # a slice keeps its leaf's noise streams
                         seeds += [a_seeds[2 * j], a_seeds[2 * j + 1]]
         run_adam(mine, seeds=seeds if a_seeds is not None else None, **adam_kw)
+        mark("compute", "adam_end")
         ev = torch.cuda.Event()
         ev.record(compute)
         up.push(entry.adam_region, ev)
+        mark("comm", "adam_push_end")
     fuse = prm.fuse_tail
     for b in plan.buckets:
         o_mode = b.index in entry.o_regions
         ids = [i for i in b.leaves if plan.owner[i] == ctx.rank]
+        mark("compute", f"ns{b.index}")
         if ids:
             sub = [ml[i] for i in ids]
             if o_mode:  # O (16-bit, leaf layout) into the exchanged buffer; the tail comes after the exchange
@@ -606,22 +615,29 @@ def sharded_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, lr: float, 
             prm.fuse_tail = 0 if o_mode else fuse
             run_muon_table(arr, len(ids), prm, dev)
             prm.fuse_tail = fuse
+        mark("compute", f"ns_end{b.index}")
         ev = torch.cuda.Event()
         ev.record(compute)
         up.push(b.index, ev, o_region=o_mode)
+        mark("comm", f"push_end{b.index}")
     # Tails of the O buckets (every rank, the owners' own leaves too, so all
     # replicas hold identical updates), each behind its bucket's arrival.
     for b in plan.buckets:
         if b.index not in entry.o_regions:
             continue
         up.wait_region(b.index, compute)
+        mark("compute", f"tail{b.index}")
         items = []
         for i in b.leaves:
             L, o = ml[i], entry.muon_offsets[i]
             p = L.p.reshape(-1) if (L.p is not None and decays[i] != 0.0) else None
             items.append((up.o_view(o, L.out.numel()), p, L.out.view(-1), scales[i], decays[i], decay_f32[i]))
         run_tail(items, lr)
+        mark("compute", f"tail_end{b.index}")
     up.finish(compute)
+    mark("compute", "finish")
+    if trace is not None:
+        trace.report(ctx.rank, [sum(ml[i].out.numel() for i in b.leaves) for b in plan.buckets])
     ctx.owned_state = owned
     adam_parts = []
     if a_items:
@@ -680,7 +696,8 @@ def ownership(params, muon_weight_dimension_numbers=None, world_size: int | None
     return tree_unflatten(treedef, out)
 
 
-def owned_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds=None):
+def owned_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds=None,
+                 a_pos=()):
     """``updates="owned"``: momentum + Newton-Schulz + fused tail for the Muon
     leaves this rank owns and AdamW for the AdamW leaves it owns, into fresh
     float32 buffers; every other leaf's update is a meta tensor.  No data
@@ -718,7 +735,8 @@ def owned_update(ctx: ShardContext, ml, prm, cbuf, scales, decays, decay_f32, a_
         a_outs.append(o)
     run_adam(items, seeds=seeds if a_seeds is not None else None, **adam_kw)
     ctx.owned_state = []
-    ctx.last_parts = (tuple(L.pos for L, r in zip(ml, mo) if r == ctx.rank), ())
+    ctx.last_parts = (tuple(L.pos for L, r in zip(ml, mo) if r == ctx.rank),
+                      tuple((pos, 0, it[0].numel()) for pos, it, r in zip(a_pos, a_items, ao) if r == ctx.rank))
     return outs, a_outs
 
 

@@ -623,7 +623,8 @@ def muon(learning_rate, ns_coeffs=_DEFAULT_NS_COEFFS, ns_steps=5, beta=0.95, eps
             a_apply = [mode_seed(pos, ps[pos]) for pos in a_pos]
         res = None
         if owned_only:
-            res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds)
+            res = distributed.owned_update(ctx, ml, prm, cbuf, scales, decays, decay_f32, a_items, adam_kw, a_seeds,
+                                           a_pos)
         elif sharded and ctx.owner_tail and ctx.transport in ("ce", "auto") and not adaptive and (ml or a_items):
             res = distributed.sharded_update(ctx, ml, prm, cbuf, scales, decays, lr, decay_f32, a_items, adam_kw,
                                              a_seeds, a_pos)
