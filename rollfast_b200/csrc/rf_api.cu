@@ -254,8 +254,8 @@ static rf_status prepare_norms(const Plan& P, const std::vector<int>& ids, const
         ml.scale_index = lp.scale_index;
         ml.chunks_per_mat = int32_t(chunks_per_mat(ml.numel));
         const size_t ge = dtype_size(gdt);
-        ml.vec_ok = lp.mu && (ml.numel % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.g) % 16 == 0) &&
-                    (reinterpret_cast<uintptr_t>(lp.mu) % 16 == 0) && ((ml.numel * int64_t(ge)) % 16 == 0);
+        ml.vec_ok = (ml.numel % 8 == 0) && (reinterpret_cast<uintptr_t>(lp.g) % 16 == 0) &&
+                    (!lp.mu || reinterpret_cast<uintptr_t>(lp.mu) % 16 == 0) && ((ml.numel * int64_t(ge)) % 16 == 0);
         chunks += lp.batch * ml.chunks_per_mat;
         mats += lp.batch;
       }

@@ -185,6 +185,17 @@ __global__ void __launch_bounds__(kEwThreads) k_momentum_sumsq(const __grid_cons
           acc = fmaf(d, d, acc);
         }
       }
+    } else if (L.vec_ok && !L.mu) {
+      // No momentum (the orthogonalize_fn seam): sum of squares of the input.
+      for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
+        float g[8];
+        GradVec<GDT>::load8(L.g, base + i, g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float d = direction(P.c, g[k], 0.f);
+          acc = fmaf(d, d, acc);
+        }
+      }
     } else if (L.vec_ok) {
       for (int64_t i = lo + int64_t(threadIdx.x) * 8; i < hi; i += int64_t(blockDim.x) * 8) {
         float g[8], m[8];

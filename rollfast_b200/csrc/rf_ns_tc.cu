@@ -249,6 +249,54 @@ __device__ __forceinline__ void load_aux_chunk(const NsGemmArgs& a, bool sym, in
   for (int q = 0; q < 4; ++q) x[q] = p[q];
 }
 
+// 16-bit output blocks through the warp's shared staging buffer.  A lane
+// holds one row of a 32x32 block (32 values in packed[]); stored directly,
+// each store instruction would touch 32 rows.  Staged (17 words per row:
+// conflict-free row writes and column gathers), the block leaves in 16-byte
+// pieces that cover 8 rows per instruction, and its transpose (the mirrored
+// block of a symmetric stage) in 4 such instructions instead of 32 2-byte
+// stores.
+__device__ __forceinline__ void stage_block16(uint32_t* s, int lane, const uint4 (&p)[4]) {
+  __syncwarp();  // every lane has finished reading the previous block
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    s[lane * 17 + 4 * q + 0] = p[q].x;
+    s[lane * 17 + 4 * q + 1] = p[q].y;
+    s[lane * 17 + 4 * q + 2] = p[q].z;
+    s[lane * 17 + 4 * q + 3] = p[q].w;
+  }
+  __syncwarp();
+}
+// Rows 0..31 of the staged block to out16[base + i * ldc + (0..31)].
+__device__ __forceinline__ void store_block16(uint16_t* out16, int64_t base, int64_t ldc, const uint32_t* s,
+                                              int lane) {
+  const int q = lane & 3;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int i = t * 8 + (lane >> 2);
+    const uint32_t* r = s + i * 17 + q * 4;
+    *reinterpret_cast<uint4*>(out16 + base + int64_t(i) * ldc + q * 8) = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+}
+// Column j of the staged block to out16[base + j * ldc + (0..31)].
+__device__ __forceinline__ void store_block16_t(uint16_t* out16, int64_t base, int64_t ldc, const uint32_t* s,
+                                                int lane) {
+  const int q = lane & 3;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int j = t * 8 + (lane >> 2);
+    const int sh = (j & 1) * 16;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = (s[(q * 8 + 2 * e) * 17 + (j >> 1)] >> sh) & 0xFFFFu;
+      const uint32_t hi = (s[(q * 8 + 2 * e + 1) * 17 + (j >> 1)] >> sh) & 0xFFFFu;
+      w[e] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(out16 + base + int64_t(j) * ldc + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // One 32-column chunk of the epilogue.  The calling warp holds rows
 // row0..row0+31 (lane = row - row0) of matrix g, columns col0..col0+31 of the
 // accumulator in v[] and, for the stages with a second operand, that
@@ -280,6 +328,16 @@ __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, in
 #pragma unroll
     for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
     uint16_t* out16 = reinterpret_cast<uint16_t*>(out);
+    if (col0 > row0) {
+      // Above the diagonal (the same for every lane: row0 and col0 are
+      // multiples of 32): the block and its mirror, staged.
+      uint32_t* s32 = reinterpret_cast<uint32_t*>(stg);
+      stage_block16(s32, lane, packed);
+      store_block16(out16, mat_off + row0 * ldc + col0, ldc, s32, lane);
+      store_block16_t(out16, mat_off + col0 * ldc + row0, ldc, s32, lane);
+      return;
+    }
+    // The diagonal block: upper triangle and mirror element by element.
     if (col0 >= row) {
       uint4* op = reinterpret_cast<uint4*>(out + rbase);
 #pragma unroll
@@ -301,9 +359,12 @@ __device__ __forceinline__ void epilogue_chunk(const NsGemmArgs& a, bool sym, in
 #pragma unroll
   for (int k = 0; k < 32; ++k) f[k] = fmaf(a.alpha, v[k], a.beta * f[k]);
   if (a.stage == kGemmBX) {
-    uint4* op = reinterpret_cast<uint4*>(out + rbase);
+    uint4 packed[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) op[q] = Vec16<T>::pack(f + 8 * q);
+    for (int q = 0; q < 4; ++q) packed[q] = Vec16<T>::pack(f + 8 * q);
+    uint32_t* s32 = reinterpret_cast<uint32_t*>(stg);
+    stage_block16(s32, lane, packed);
+    store_block16(reinterpret_cast<uint16_t*>(out), mat_off + row0 * ldc + col0, ldc, s32, lane);
     return;
   }
   const FinalLeaf& L = a.final_leaf[fl];
