@@ -647,9 +647,10 @@ def main():
     if owned_mode and world > 1:
         transport = ", owners keep their leaves' updates (no exchange: the float32 update tree does not fit a GPU)"
     grad_gb = sum(math.prod(s) for s in leaves_of(shapes)) * 2 / 1e9  # one bf16 gradient set
-    # The traffic figure comes from a capture of the Llama-3-8B 4096x14336
-    # sub-batch launches; other workloads' launches hold other shapes.
-    traffic = TRAFFIC_PER_LAUNCH if (full_size and args.workload == "llama3_8b_muon_step") else None
+    # The traffic figure comes from a capture of the one-GPU Llama-3-8B
+    # 4096x14336 sub-batch launches; other workloads' launches, and sharded
+    # ones (a rank's own leaves only), hold other matrices.
+    traffic = TRAFFIC_PER_LAUNCH if (full_size and args.workload == "llama3_8b_muon_step" and world == 1) else None
 
     if rank == 0:
         out = {
