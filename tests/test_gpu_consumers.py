@@ -1,5 +1,5 @@
 """The Newton-Schulz kernels behind the reference's other Muon consumers
-(the orthogonalize_fn seam, SURVEY row f1), each exercised with the exact
+(the orthogonalize_fn seam), each exercised with the exact
 call it makes, against the oracle:
 
   * NorMuon (src/rollfast/optim/normuon.py:82-97, called at 165-174) and

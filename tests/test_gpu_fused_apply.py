@@ -1,4 +1,4 @@
-"""The parameter apply fused into the update (SURVEY row f2): for
+"""The parameter apply fused into the update: for
 ``rollfast_b200.muon(...)``, ``update_and_apply`` writes p + u from the
 Newton-Schulz final epilogue and the AdamW kernel (the float32 update is never
 stored) and must equal ``tx.update`` followed by ``apply_updates``
